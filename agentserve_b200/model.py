@@ -1,0 +1,395 @@
+"""Llama decoder whose attention step runs on the sm_100a C-ABI kernels.
+
+Drop-in for the object AgentServe's Engine calls (agentserve/model/llama.py):
+same parameter names and shapes as LlamaModel (llama.py:245-262), and the three
+methods Engine uses:
+
+  forward(token_ids, kv_cache, position_offset)        llama.py:478-520, engine.py:304-308
+  forward_decode_batch(last_token_ids, kv_caches, pos)  llama.py:265-376, engine.py:370-374
+  forward_decode_paged(last, seq_lens, pos, allocator, request_ids)
+                                                        llama.py:379-475, engine.py:360-366
+
+Attention, RoPE, KV writes, packing and block gathers are the library's kernels;
+norms, projections (cuBLAS through torch), SwiGLU, lm_head and greedy argmax stay
+torch ops, as in the reference.  With reference_compat=True (default) two
+behaviours of the reference's decode paths are reproduced so results match it:
+the decode attention output is flattened dim-major before o_proj (llama.py:362,
+470), and forward_decode_batch returns, for every sequence shorter than the
+batch's longest, a zero K/V row in place of its new token (llama.py:327, 372).
+reference_compat=False gives the head-major flatten of prefill (llama.py:184) and
+keeps the new token's K/V.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Sequence
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _native as N
+from . import ops
+from .cache import DeviceBlockAllocator
+
+BS = ops.BLOCK_SIZE
+
+
+def precompute_rope_freqs(head_dim: int, max_seq_len: int, theta: float) -> torch.Tensor:
+    """fp32 cos||sin table [max_seq_len, head_dim] (llama.py:63-77), built on the CPU
+    so every device gets the same bits."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    f = torch.outer(torch.arange(max_seq_len, dtype=torch.float32), inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1)
+
+
+class RMSNorm(nn.Module):
+    """llama.py:39-56."""
+
+    def __init__(self, dim: int, eps: float = 1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        r = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
+        return (xf * r).to(x.dtype) * self.weight
+
+
+class _Attn(nn.Module):
+    def __init__(self, c):
+        super().__init__()
+        H, Kh, D = c.n_heads, c.n_kv_heads, c.head_dim
+        self.q_proj = nn.Linear(c.hidden_dim, H * D, bias=False)
+        self.k_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
+        self.v_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
+        self.o_proj = nn.Linear(H * D, c.hidden_dim, bias=False)
+
+
+class _MLP(nn.Module):
+    def __init__(self, c):
+        super().__init__()
+        self.gate_proj = nn.Linear(c.hidden_dim, c.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(c.hidden_dim, c.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(c.intermediate_size, c.hidden_dim, bias=False)
+
+
+class _Layer(nn.Module):
+    def __init__(self, c):
+        super().__init__()
+        self.attn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
+        self.attn = _Attn(c)
+        self.ffn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
+        self.ffn = _MLP(c)
+
+
+class B200LlamaModel(nn.Module):
+    def __init__(self, config, dtype: torch.dtype = torch.bfloat16,
+                 device: str | torch.device = "cuda", fused_projections: bool = True,
+                 reference_compat: bool = True):
+        super().__init__()
+        c = self.config = config
+        self.H, self.Kh, self.D = c.n_heads, c.n_kv_heads, c.head_dim
+        self.embed = nn.Embedding(c.vocab_size, c.hidden_dim)
+        self.layers = nn.ModuleList([_Layer(c) for _ in range(c.n_layers)])
+        self.norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
+        self.lm_head = nn.Linear(c.hidden_dim, c.vocab_size, bias=False)
+        self.to(device=device, dtype=dtype)
+        # fp32 table whatever the model dtype (the reference's table is fp32 unless the
+        # whole module is cast, llama.py:261-262)
+        self.rope_table = precompute_rope_freqs(self.D, c.max_seq_len, c.rope_theta).to(device)
+        self.scale = 1.0 / math.sqrt(self.D)  # SDPA's default scale (llama.py:183)
+        self.fused_projections = fused_projections
+        self.reference_compat = reference_compat
+        self.decode_layout = N.AS_LAYOUT_DIM_MAJOR if reference_compat else N.AS_LAYOUT_HEAD_MAJOR
+        self._fused = False
+        self._workspaces = {}
+        # split-K chunk (16-token blocks) for decode attention; None picks it per call
+        self.decode_blocks_per_split: Optional[int] = None
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.weight.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.embed.weight.dtype
+
+    # ------------------------------------------------------------------ weights
+    @torch.no_grad()
+    def fuse_projections_(self) -> None:
+        """Store q/k/v and gate/up weights in one tensor each and point the Linear
+        weights at views of it (state dict names unchanged), so one GEMM serves q, k, v
+        and one serves gate, up."""
+        if self._fused or not self.fused_projections:
+            return
+        for layer in self.layers:
+            a, f = layer.attn, layer.ffn
+            qkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+            nq, nk = a.q_proj.weight.shape[0], a.k_proj.weight.shape[0]
+            a.q_proj.weight = nn.Parameter(qkv[:nq], requires_grad=False)
+            a.k_proj.weight = nn.Parameter(qkv[nq:nq + nk], requires_grad=False)
+            a.v_proj.weight = nn.Parameter(qkv[nq + nk:], requires_grad=False)
+            a._qkv_w = qkv
+            gu = torch.cat([f.gate_proj.weight, f.up_proj.weight], 0).contiguous()
+            ni = f.gate_proj.weight.shape[0]
+            f.gate_proj.weight = nn.Parameter(gu[:ni], requires_grad=False)
+            f.up_proj.weight = nn.Parameter(gu[ni:], requires_grad=False)
+            f._gu_w = gu
+        self._fused = True
+
+    def _qkv(self, layer: _Layer, h: torch.Tensor):
+        n = h.shape[0]
+        H, Kh, D = self.H, self.Kh, self.D
+        a = layer.attn
+        if self.fused_projections:
+            qkv = F.linear(h, a._qkv_w)
+            return (qkv[:, :H * D].view(n, H, D), qkv[:, H * D:(H + Kh) * D].view(n, Kh, D),
+                    qkv[:, (H + Kh) * D:].view(n, Kh, D))
+        return (a.q_proj(h).view(n, H, D), a.k_proj(h).view(n, Kh, D), a.v_proj(h).view(n, Kh, D))
+
+    def _mlp(self, layer: _Layer, x: torch.Tensor) -> torch.Tensor:
+        f = layer.ffn
+        h = layer.ffn_norm(x)
+        if self.fused_projections:
+            gu = F.linear(h, f._gu_w)
+            i = gu.shape[1] // 2
+            return f.down_proj(F.silu(gu[:, :i]) * gu[:, i:])
+        return f.down_proj(F.silu(f.gate_proj(h)) * f.up_proj(h))
+
+    def _logits(self, x: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(self.norm(x))
+
+    def _workspace(self, B: int, max_blocks: int, bps: int) -> torch.Tensor:
+        ws = self._workspaces.get(self.device)
+        if ws is None:
+            ws = self._workspaces[self.device] = ops.DecodeWorkspace(self.H, self.Kh, self.D,
+                                                                     self.device)
+        return ws.get(B, max_blocks, bps)
+
+    # ------------------------------------------------------------------ prefill
+    @torch.inference_mode()
+    def forward(self, token_ids, kv_cache=None, position_offset: int = 0):
+        """Prefill T tokens after an optional cached prefix (llama.py:478-520).
+
+        kv_cache: per-layer (k, v) [P, Kh, D] (the reference's list format) or None.
+        Returns (logits [T, V], per-layer (k, v) [P+T, Kh, D]).  Each layer's K/V sit
+        in a contiguous 16-token-block buffer that the prefill kernel reads as a pool
+        with an identity block table; the returned tensors are views of it."""
+        self.fuse_projections_()
+        dev = self.device
+        if not isinstance(token_ids, torch.Tensor):
+            token_ids = torch.tensor(token_ids, dtype=torch.long)
+        token_ids = token_ids.to(dev, non_blocking=True)
+        T = int(token_ids.shape[0])
+        # Attention covers the given prefix K/V plus the new tokens; position_offset only
+        # drives RoPE (llama.py:506-507), exactly as in the reference, where a call with
+        # kv_cache=None and an offset attends over the new tokens alone.
+        P = int(kv_cache[0][0].shape[0]) if kv_cache is not None else 0
+        total = P + T
+        nblk = (total + BS - 1) // BS
+        x = self.embed(token_ids)
+        pos = torch.arange(position_offset, position_offset + T, device=dev, dtype=torch.int64)
+        slots = torch.arange(P, total, device=dev, dtype=torch.int64)
+        bt = torch.arange(nblk, dtype=torch.int32, device=dev).view(1, nblk)
+        cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        lk = torch.tensor([total], dtype=torch.int32, device=dev)
+        new_cache = []
+        for li, layer in enumerate(self.layers):
+            kbuf = torch.empty(nblk, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
+            vbuf = torch.empty_like(kbuf)
+            kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
+            if P:
+                kf[:P].copy_(kv_cache[li][0])
+                vf[:P].copy_(kv_cache[li][1])
+            h = layer.attn_norm(x)
+            q, k, v = self._qkv(layer, h)
+            ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
+            attn = ops.varlen_prefill_attention(q, kbuf, vbuf, bt, cu, lk, T, self.scale)
+            x = x + layer.attn.o_proj(attn)
+            x = x + self._mlp(layer, x)
+            new_cache.append((kf[:total], vf[:total]))
+        return self._logits(x), new_cache
+
+    # ------------------------------------------------------------------ decode (lists)
+    @torch.inference_mode()
+    def forward_decode_batch(self, last_token_ids: List[int], kv_caches: list,
+                             position_offsets: List[int]):
+        """llama.py:265-376 with the per-request KV lists packed into one block buffer
+        per layer (each sequence gets its own 16-token blocks), the new token written
+        by the fused RoPE kernel and attention done by the paged decode kernel."""
+        self.fuse_projections_()
+        B = len(last_token_ids)
+        c = self.config
+        if B == 0:
+            return torch.zeros(0, c.vocab_size), []
+        dev = self.device
+        lens = [int(kv_caches[b][0][0].shape[0]) for b in range(B)]
+        max_len = max(lens)
+        nb = [(L + 1 + BS - 1) // BS for L in lens]
+        starts = [0]
+        for n in nb[:-1]:
+            starts.append(starts[-1] + n)
+        total_blocks = starts[-1] + nb[-1]
+        mb = max(nb)
+        bt_host = torch.zeros(B, mb, dtype=torch.int32)
+        for b in range(B):
+            bt_host[b, :nb[b]] = torch.arange(starts[b], starts[b] + nb[b], dtype=torch.int32)
+        bt = bt_host.to(dev)
+        slots_host = [starts[b] * BS + lens[b] for b in range(B)]
+        slots = torch.tensor(slots_host, dtype=torch.int64, device=dev)
+        pos = torch.tensor(position_offsets, dtype=torch.int64, device=dev)
+        lk = torch.tensor([L + 1 for L in lens], dtype=torch.int32, device=dev)
+        bps = ops.choose_blocks_per_split(total_blocks, B, self.Kh, mb)
+        ws = self._workspace(B, mb, bps)
+        x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
+        new = [[] for _ in range(B)]
+        short = [b for b in range(B) if lens[b] < max_len]
+        for li, layer in enumerate(self.layers):
+            kbuf = torch.zeros(total_blocks, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
+            vbuf = torch.zeros_like(kbuf)
+            kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
+            for b in range(B):
+                s = starts[b] * BS
+                kf[s:s + lens[b]].copy_(kv_caches[b][li][0])
+                vf[s:s + lens[b]].copy_(kv_caches[b][li][1])
+            h = layer.attn_norm(x)
+            q, k, v = self._qkv(layer, h)
+            ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
+            attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,
+                                              out_layout=self.decode_layout)
+            x = x + layer.attn.o_proj(attn)
+            x = x + self._mlp(layer, x)
+            if self.reference_compat and short:
+                idx = torch.tensor([slots_host[b] for b in short], device=dev)
+                kf[idx] = 0
+                vf[idx] = 0
+            for b in range(B):
+                s = starts[b] * BS
+                new[b].append((kf[s:s + lens[b] + 1], vf[s:s + lens[b] + 1]))
+        return self._logits(x), new
+
+    # ------------------------------------------------------------------ decode (paged)
+    def _decode_core(self, tokens: torch.Tensor, seq_lens: torch.Tensor, row_ids: torch.Tensor,
+                     allocator: DeviceBlockAllocator, max_blocks: int, bps: int,
+                     positions: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One decode step entirely on the device (no host sync): pack -> per layer
+        (norm, fused QKV GEMM, fused RoPE+cache write, paged attention, o_proj,
+        MLP) -> norm -> lm_head.  Returns logits [B, V]."""
+        B = tokens.shape[0]
+        pk = ops.pack_decode(allocator.block_tables, seq_lens, row_ids, max_blocks)
+        pos = pk.positions if positions is None else positions
+        ws = self._workspace(B, max_blocks, bps)
+        x = self.embed(tokens)
+        for li, layer in enumerate(self.layers):
+            h = layer.attn_norm(x)
+            q, k, v = self._qkv(layer, h)
+            kp, vp = allocator.k_plane(li), allocator.v_plane(li)
+            ops.rope_reshape_and_cache(q, k, v, pos, pk.slot_mapping, self.rope_table, kp, vp)
+            attn = ops.paged_decode_attention(q, kp, vp, pk.block_tables, pk.seq_lens_k,
+                                              self.scale, bps, ws, out_layout=self.decode_layout)
+            x = x + layer.attn.o_proj(attn)
+            x = x + self._mlp(layer, x)
+        return self._logits(x)
+
+    @torch.inference_mode()
+    def forward_decode_paged(self, last_token_ids: List[int], seq_lens: List[int],
+                             position_offsets: List[int], allocator, request_ids: List[str]):
+        """llama.py:379-475: K/V read in place from the allocator's device pool through
+        its device block table; the new token's K/V is written by the fused RoPE kernel
+        (write_kv_decode, llama.py:437-439).  Returns (logits [B, V], None)."""
+        if not isinstance(allocator, DeviceBlockAllocator):
+            raise TypeError("forward_decode_paged needs an agentserve_b200.DeviceBlockAllocator "
+                            "(a device-resident pool and block table)")
+        self.fuse_projections_()
+        B = len(last_token_ids)
+        if B == 0:
+            return torch.zeros(0, self.config.vocab_size), None
+        dev = self.device
+        rows = allocator.rows_for(request_ids)
+        host = torch.tensor([list(last_token_ids), list(seq_lens), rows, list(position_offsets)],
+                            dtype=torch.int64).pin_memory()
+        d = host.to(dev, non_blocking=True)
+        tokens = d[0]
+        sl = d[1].to(torch.int32)
+        rid = d[2].to(torch.int32)
+        pos = None if list(position_offsets) == list(seq_lens) else d[3].contiguous()
+        max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
+        bps = self.decode_blocks_per_split
+        if bps is None:
+            total = sum((L + 1 + BS - 1) // BS for L in seq_lens)
+            bps = ops.choose_blocks_per_split(total, B, self.Kh, max_blocks)
+        logits = self._decode_core(tokens, sl, rid, allocator, max_blocks, bps, positions=pos)
+        return logits, None
+
+
+def greedy(logits: torch.Tensor) -> torch.Tensor:
+    """sampling.py:46-58 with temperature <= 1e-6: fp32, nan_to_num, argmax."""
+    lf = torch.nan_to_num(logits.float(), nan=0.0, posinf=1e4, neginf=-1e4)
+    return lf.argmax(dim=-1)
+
+
+class DecodeGraph:
+    """One greedy decode step for a fixed batch, captured in a CUDA graph.
+
+    Static device inputs: tokens [B] int64, seq_lens [B] int32 (cached tokens = position
+    of the new token), row_ids [B] int32 (allocator table rows).  Output: next_tokens
+    [B] int64.  With advance=True the graph also feeds next_tokens back into tokens and
+    increments seq_lens, so replays run consecutive decode steps with no host work.
+    """
+
+    def __init__(self, model: B200LlamaModel, allocator: DeviceBlockAllocator, batch_size: int,
+                 max_blocks: int, blocks_per_split: int, advance: bool = False):
+        self.model = model
+        self.allocator = allocator
+        self.B = batch_size
+        self.max_blocks = max_blocks
+        self.bps = blocks_per_split
+        self.advance = advance
+        dev = model.device
+        self.tokens = torch.zeros(batch_size, dtype=torch.int64, device=dev)
+        self.seq_lens = torch.zeros(batch_size, dtype=torch.int32, device=dev)
+        self.row_ids = torch.zeros(batch_size, dtype=torch.int32, device=dev)
+        self.next_tokens = torch.zeros(batch_size, dtype=torch.int64, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    def _body(self):
+        m = self.model
+        logits = m._decode_core(self.tokens, self.seq_lens, self.row_ids, self.allocator,
+                                self.max_blocks, self.bps)
+        self.next_tokens.copy_(greedy(logits))
+        if self.advance:
+            self.tokens.copy_(self.next_tokens)
+            self.seq_lens.add_(1)
+
+    @torch.inference_mode()
+    def capture(self, tokens, seq_lens, row_ids) -> None:
+        """Warm up on a side stream (sets kernel attributes, cuBLAS handles) then
+        capture.  The warm-up writes one token per sequence into the pool at
+        seq_lens; the caller's next step overwrites the same slots."""
+        self.model.fuse_projections_()
+        self.load(tokens, seq_lens, row_ids)
+        s = torch.cuda.Stream(device=self.model.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            saved = (self.tokens.clone(), self.seq_lens.clone())
+            self._body()
+            self.tokens.copy_(saved[0])
+            self.seq_lens.copy_(saved[1])
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        torch.cuda.synchronize()
+
+    def load(self, tokens, seq_lens, row_ids) -> None:
+        self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int64), non_blocking=True)
+        self.seq_lens.copy_(torch.as_tensor(seq_lens, dtype=torch.int32), non_blocking=True)
+        self.row_ids.copy_(torch.as_tensor(row_ids, dtype=torch.int32), non_blocking=True)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.next_tokens

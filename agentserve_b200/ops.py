@@ -1,0 +1,283 @@
+"""torch-facing wrappers of the C-ABI kernels.
+
+Each wrapper checks shapes/devices, passes raw device pointers and the current CUDA
+stream to the library, and raises on a non-zero status.  Tensors must live on a
+CUDA device: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+BLOCK_SIZE = 16
+
+_DTYPES = {torch.float32: N.AS_DTYPE_F32, torch.float16: N.AS_DTYPE_F16,
+           torch.bfloat16: N.AS_DTYPE_BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}; use float32, float16 or bfloat16") from None
+
+
+def _cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("agentserve_b200 ops need CUDA tensors (no CPU fallback)")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_status(clear: bool = True, device=None) -> int:
+    """Read (and clear) the device status word: 1 bad block id, 2 bad slot, 4 wait
+    timeout, 8 position outside the RoPE table, 16 sequence longer than its table row."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    bits = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        N.check(N.load().as_device_status(int(clear), ctypes.byref(bits), _stream(dev)),
+                "as_device_status")
+    return bits.value
+
+
+# ---------------------------------------------------------------------------
+# (1) packing
+# ---------------------------------------------------------------------------
+@dataclass
+class DecodePack:
+    positions: torch.Tensor     # [B] int64
+    slot_mapping: torch.Tensor  # [B] int64
+    seq_lens_k: torch.Tensor    # [B] int32
+    cu_seqlens_q: torch.Tensor  # [B+1] int32
+    block_tables: torch.Tensor  # [B, max_blocks] int32
+
+
+@dataclass
+class PrefillPack:
+    cu_seqlens_q: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    seq_lens_k: torch.Tensor
+    block_tables: torch.Tensor
+
+
+def pack_decode(block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                row_ids: Optional[torch.Tensor] = None, max_blocks: Optional[int] = None,
+                out: Optional[DecodePack] = None) -> DecodePack:
+    """block_tables [rows, stride] int32 (device-resident allocator table),
+    seq_lens [B] int32 = cached tokens (position of the new token), row_ids [B] int32."""
+    _cuda(block_tables, seq_lens, row_ids)
+    B = seq_lens.shape[0]
+    mb = max_blocks if max_blocks is not None else block_tables.shape[1]
+    dev = seq_lens.device
+    if out is None:
+        out = DecodePack(torch.empty(B, dtype=torch.int64, device=dev),
+                         torch.empty(B, dtype=torch.int64, device=dev),
+                         torch.empty(B, dtype=torch.int32, device=dev),
+                         torch.empty(B + 1, dtype=torch.int32, device=dev),
+                         torch.empty(B, mb, dtype=torch.int32, device=dev))
+    assert block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32
+    assert block_tables.stride(1) == 1
+    N.check(N.load().as_pack_decode(
+        _ptr(block_tables), block_tables.stride(0), _ptr(row_ids), _ptr(seq_lens), B, mb,
+        BLOCK_SIZE, _ptr(out.positions), _ptr(out.slot_mapping), _ptr(out.seq_lens_k),
+        _ptr(out.cu_seqlens_q), _ptr(out.block_tables), _stream(dev)), "as_pack_decode")
+    return out
+
+
+def pack_prefill(block_tables: torch.Tensor, num_cached: torch.Tensor, num_new: torch.Tensor,
+                 total_new: int, row_ids: Optional[torch.Tensor] = None,
+                 max_blocks: Optional[int] = None) -> PrefillPack:
+    _cuda(block_tables, num_cached, num_new, row_ids)
+    R = num_new.shape[0]
+    mb = max_blocks if max_blocks is not None else block_tables.shape[1]
+    dev = num_new.device
+    out = PrefillPack(torch.empty(R + 1, dtype=torch.int32, device=dev),
+                      torch.empty(total_new, dtype=torch.int64, device=dev),
+                      torch.empty(total_new, dtype=torch.int64, device=dev),
+                      torch.empty(R, dtype=torch.int32, device=dev),
+                      torch.empty(R, mb, dtype=torch.int32, device=dev))
+    N.check(N.load().as_pack_prefill(
+        _ptr(block_tables), block_tables.stride(0), _ptr(row_ids), _ptr(num_cached),
+        _ptr(num_new), R, total_new, mb, BLOCK_SIZE, _ptr(out.cu_seqlens_q),
+        _ptr(out.positions), _ptr(out.slot_mapping), _ptr(out.seq_lens_k),
+        _ptr(out.block_tables), _stream(dev)), "as_pack_prefill")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (2) fused RoPE + reshape_and_cache
+# ---------------------------------------------------------------------------
+def _row_view_ok(x: torch.Tensor) -> bool:
+    return x.dim() == 3 and x.stride(2) == 1 and x.stride(1) == x.shape[2]
+
+
+def rope_reshape_and_cache(q: Optional[torch.Tensor], k: torch.Tensor, v: torch.Tensor,
+                           positions: Optional[torch.Tensor], slot_mapping: torch.Tensor,
+                           cos_sin: Optional[torch.Tensor], k_cache: torch.Tensor,
+                           v_cache: torch.Tensor, k_out: Optional[torch.Tensor] = None) -> None:
+    """q [T, H, D] (rotated in place), k/v [T, Kh, D]; each may be a row-strided view
+    (e.g. column slices of a fused QKV output).  k_cache/v_cache [NB, 16, Kh, D].
+    cos_sin None: no rotation (plain write of k and v)."""
+    _cuda(q, k, v, positions, slot_mapping, cos_sin, k_cache, v_cache, k_out)
+    T, Kh, D = k.shape
+    H = q.shape[1] if q is not None else 1
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t is not None and not _row_view_ok(t):
+            raise ValueError(f"{name} must be [T, heads, D] with contiguous rows")
+    if cos_sin is not None:
+        assert cos_sin.dtype == torch.float32 and cos_sin.is_contiguous()
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert k_cache.shape[1:] == (BLOCK_SIZE, Kh, D), "k_cache must be [NB, 16, Kh, D]"
+    num_slots = k_cache.shape[0] * BLOCK_SIZE
+    N.check(N.load().as_rope_reshape_and_cache(
+        _ptr(q), q.stride(0) if q is not None else H * D, _ptr(k), k.stride(0), _ptr(v),
+        v.stride(0), _ptr(positions), _ptr(slot_mapping), _ptr(cos_sin),
+        cos_sin.shape[0] if cos_sin is not None else 0, _ptr(k_cache), _ptr(v_cache), num_slots,
+        _ptr(k_out), T, H, Kh, D, dtype_code(k.dtype), _stream(k.device)),
+        "as_rope_reshape_and_cache")
+
+
+# ---------------------------------------------------------------------------
+# (3) paged decode attention
+# ---------------------------------------------------------------------------
+def decode_workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                           max_blocks: int, blocks_per_split: int) -> int:
+    return int(N.load().as_paged_decode_workspace_size(num_seqs, num_heads, num_kv_heads,
+                                                        head_dim, max_blocks, blocks_per_split))
+
+
+def new_decode_workspace(num_seqs, num_heads, num_kv_heads, head_dim, max_blocks,
+                         blocks_per_split, device) -> torch.Tensor:
+    """Zero-filled workspace (the kernel keeps its counters at zero between calls)."""
+    n = decode_workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim, max_blocks,
+                               blocks_per_split)
+    return torch.zeros(max(n, 256), dtype=torch.uint8, device=device)
+
+
+class DecodeWorkspace:
+    """Grow-only split-K workspace shared by calls with different batch sizes.
+
+    The library keeps per-(sequence, head) arrival counters at the front of the
+    workspace ([B*H] int32, rounded up to 256 bytes) and split partials after them,
+    and leaves every counter it used at zero.  A call with a larger B than earlier
+    calls extends the counter region over bytes that held partials, so that region
+    is zeroed first; otherwise no memset is issued (fixed-B CUDA graphs issue none).
+    """
+
+    def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device):
+        self.H, self.Kh, self.D = num_heads, num_kv_heads, head_dim
+        self.device = device
+        self.buf: Optional[torch.Tensor] = None
+        self._clean_upto = 0  # bytes [0, _clean_upto) are known to be zero
+
+    def get(self, num_seqs: int, max_blocks: int, blocks_per_split: int) -> torch.Tensor:
+        need = decode_workspace_bytes(num_seqs, self.H, self.Kh, self.D, max_blocks,
+                                      blocks_per_split)
+        counters = (num_seqs * self.H * 4 + 255) // 256 * 256
+        if self.buf is None or self.buf.numel() < need:
+            size = max(need, 1 << 20)
+            if self.buf is not None:
+                size = max(size, 2 * self.buf.numel())
+            self.buf = torch.zeros(size, dtype=torch.uint8, device=self.device)
+            self._clean_upto = counters
+        elif counters > self._clean_upto:
+            self.buf[:counters].zero_()
+            self._clean_upto = counters
+        else:
+            self._clean_upto = counters  # partials of this call start right here
+        return self.buf
+
+
+def choose_blocks_per_split(total_blocks: int, num_seqs: int, num_kv_heads: int,
+                            max_blocks: int, num_sms: int = 148) -> int:
+    """Split-K chunk (in 16-token blocks) so that the CTAs of one call cover the SMs
+    a few times over: each CTA streams one chunk of one (sequence, KV head)."""
+    target_ctas = 4 * num_sms
+    pairs = max(1, num_seqs * num_kv_heads)
+    per_pair = max(1, total_blocks // max(1, num_seqs))
+    splits = max(1, -(-target_ctas // pairs))
+    bps = max(8, -(-per_pair // splits))
+    bps = min(bps, 256, max(8, max_blocks))
+    return int(-(-bps // 4) * 4)
+
+
+def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           block_tables: torch.Tensor, seq_lens_k: torch.Tensor, scale: float,
+                           blocks_per_split: int, workspace: Optional[torch.Tensor],
+                           out: Optional[torch.Tensor] = None,
+                           out_layout: int = N.AS_LAYOUT_HEAD_MAJOR,
+                           num_heads: Optional[int] = None) -> torch.Tensor:
+    """q [B, H, D] (row-strided view allowed), k_cache/v_cache [NB, 16, Kh, D],
+    block_tables [B, >=max_blocks] int32, seq_lens_k [B] int32 (keys incl. the new
+    token).  Returns out [B, H*D] in out_layout."""
+    _cuda(q, k_cache, v_cache, block_tables, seq_lens_k, workspace, out)
+    B, H, D = q.shape
+    NB, bs, Kh, D2 = k_cache.shape
+    assert bs == BLOCK_SIZE and D2 == D and _row_view_ok(q)
+    assert block_tables.dtype == torch.int32 and block_tables.stride(1) == 1
+    max_blocks = block_tables.shape[1]
+    if out is None:
+        out = torch.empty(B, H * D, dtype=q.dtype, device=q.device)
+    ws_ptr = _ptr(workspace)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    N.check(N.load().as_paged_decode_attention(
+        _ptr(out), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache), _ptr(block_tables),
+        block_tables.stride(0), _ptr(seq_lens_k), B, H, Kh, D, BLOCK_SIZE, NB, max_blocks,
+        float(scale), int(blocks_per_split), ws_ptr, ws_bytes, int(out_layout),
+        dtype_code(q.dtype), _stream(q.device)), "as_paged_decode_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (4) varlen prefill attention
+# ---------------------------------------------------------------------------
+def varlen_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                             block_tables: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                             seq_lens_k: torch.Tensor, max_seqlen_q: int, scale: float,
+                             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [total_q, H, D] (row-strided view allowed); returns out [total_q, H*D]
+    (head-major, as prefill flattens it: llama.py:184)."""
+    _cuda(q, k_cache, v_cache, block_tables, cu_seqlens_q, seq_lens_k, out)
+    Tq, H, D = q.shape
+    NB, bs, Kh, D2 = k_cache.shape
+    assert bs == BLOCK_SIZE and D2 == D and _row_view_ok(q)
+    assert block_tables.dtype == torch.int32 and block_tables.stride(1) == 1
+    R = seq_lens_k.shape[0]
+    if out is None:
+        out = torch.empty(Tq, H * D, dtype=q.dtype, device=q.device)
+    N.check(N.load().as_varlen_prefill_attention(
+        _ptr(out), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache), _ptr(block_tables),
+        block_tables.stride(0), _ptr(cu_seqlens_q), _ptr(seq_lens_k), R, int(max_seqlen_q), Tq,
+        H, Kh, D, BLOCK_SIZE, NB, block_tables.shape[1], float(scale), dtype_code(q.dtype),
+        _stream(q.device)), "as_varlen_prefill_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (5) block gather / copy
+# ---------------------------------------------------------------------------
+def block_copy(dst: torch.Tensor, src: torch.Tensor, src_ids: torch.Tensor,
+               dst_ids: Optional[torch.Tensor], bytes_per_block: int, num_planes: int,
+               src_plane_stride: int, dst_plane_stride: int, src_num_blocks: int,
+               dst_num_blocks: int) -> None:
+    """Byte-level block copy; strides in bytes.  See as_block_copy."""
+    _cuda(dst, src, src_ids, dst_ids)
+    n = src_ids.shape[0]
+    N.check(N.load().as_block_copy(
+        _ptr(dst), _ptr(src), _ptr(src_ids), _ptr(dst_ids), n, int(bytes_per_block),
+        int(num_planes), int(src_plane_stride), int(dst_plane_stride), int(src_num_blocks),
+        int(dst_num_blocks), _stream(dst.device)), "as_block_copy")

@@ -1,0 +1,200 @@
+/*
+ * agentserve_b200 — C ABI of the B200 (sm_100a) continuous-batching attention step.
+ *
+ * Plain C: device pointers, sizes and a cudaStream_t.  No torch types.  Every
+ * entry point is stream-ordered on the caller's stream, allocates nothing, and
+ * returns an int status (AS_OK = 0).  On failure as_last_error() gives a
+ * message for the calling host thread.  Kernels never trap: out-of-range block
+ * ids / slots / positions and bounded waits that run out set bits in a per-device
+ * status word that as_device_status() reads and clears.
+ *
+ * KV pool layout (one layer, K and V planes given separately) follows the
+ * reference's kv_pool[2, L, NB, BS, Kh, D] (agentserve/engine/cache.py:62-66):
+ *   k_cache / v_cache = &kv_pool[0|1, layer]  viewed as [NB, BS, Kh, D],
+ *   slot s = block_id * BS + offset  addresses row s of [NB*BS, Kh, D].
+ * BS (block_size) must be 16 (the reference default, engine.py:86).
+ *
+ * Reference interfaces replaced (file:line inside krishs0404/agentserve):
+ *   as_pack_decode            engine.py:349-357 + llama.py:408-411 (host lists -> tensors)
+ *                             + cache.py:152-154 (slot of the decode token)
+ *   as_pack_prefill           engine.py:299-307 + cache.py:134-140 (slots of prompt tokens)
+ *   as_rope_reshape_and_cache llama.py:80-99 (apply_rope on q,k) + cache.py:125-156
+ *                             (write_kv_prefill / write_kv_decode)
+ *   as_paged_decode_attention llama.py:419-469 (gather_kv -> pad -> GQA expand -> SDPA)
+ *                             and llama.py:303-361 (padded-list decode)
+ *   as_varlen_prefill_attention llama.py:128-186 (prefill over cached prefix + new tokens)
+ *   as_block_copy             cache.py:158-189 (gather_kv) and engine.py:274-281,338-345
+ *                             (prefix-cache KV clone / seed)
+ */
+#ifndef AGENTSERVE_B200_H_
+#define AGENTSERVE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AS_API __attribute__((visibility("default")))
+#else
+#define AS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* as_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+/* status codes */
+#define AS_OK 0
+#define AS_ERR_INVALID_ARG 1
+#define AS_ERR_UNSUPPORTED 2
+#define AS_ERR_CUDA 3
+#define AS_ERR_WORKSPACE 4
+
+/* layouts of the decode attention output [B, H*D] */
+#define AS_LAYOUT_HEAD_MAJOR 0 /* out[b, h*D + d] (prefill's flatten, llama.py:184) */
+#define AS_LAYOUT_DIM_MAJOR 1  /* out[b, d*H + h] (the reference decode paths' flatten,
+                                  SDPA out .transpose(1, 2).reshape(B, H*D), llama.py:362,470) */
+
+/* element types of q / k / v / out / KV pool */
+#define AS_DTYPE_F32 0
+#define AS_DTYPE_F16 1
+#define AS_DTYPE_BF16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+AS_API int as_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+AS_API const char* as_last_error(void);
+
+/* Read (and clear when clear != 0) the device status word of the current device.
+ * Synchronises `stream`.  Bits: 1 bad block id, 2 bad slot, 4 wait timeout,
+ * 8 RoPE position outside the table, 16 sequence longer than its block-table row. */
+AS_API int as_device_status(int clear, int* out_bits, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (1) Ragged-batch packing                                                  */
+/* ------------------------------------------------------------------------- */
+
+/* Decode batch of B sequences.  Inputs:
+ *   block_tables [*, bt_stride] int32 — device-resident table rows of the allocator
+ *   row_ids      [B] int32            — table row of each sequence (NULL: row b)
+ *   seq_lens     [B] int32            — tokens already cached = position of the new token
+ *                                       (engine.py:350,356: num_cached + num_out - 1)
+ * Outputs (all device):
+ *   positions    [B]    int64  = seq_lens
+ *   slot_mapping [B]    int64  = bt[row][pos/16]*16 + pos%16    (cache.py:152-154)
+ *   seq_lens_k   [B]    int32  = seq_lens + 1 (keys visible to the new token)
+ *   cu_seqlens_q [B+1]  int32  = 0,1,...,B
+ *   packed_bt    [B, max_blocks] int32 — rows gathered (NULL to skip)
+ */
+AS_API int as_pack_decode(const int32_t* block_tables, int64_t bt_stride, const int32_t* row_ids,
+                   const int32_t* seq_lens, int32_t num_seqs, int32_t max_blocks,
+                   int32_t block_size, int64_t* positions, int64_t* slot_mapping,
+                   int32_t* seq_lens_k, int32_t* cu_seqlens_q, int32_t* packed_bt,
+                   as_stream_t stream);
+
+/* Varlen prefill batch of R sequences with num_cached[r] tokens already in the
+ * pool (prefix-cache hit, engine.py:275-276) and num_new[r] new tokens.
+ * Outputs: cu_seqlens_q [R+1] (prefix sum of num_new), positions/slot_mapping
+ * [total_new] int64 (position num_cached+i, cache.py:136-140), seq_lens_k [R] =
+ * num_cached + num_new, packed_bt [R, max_blocks] (NULL to skip).  total_new must
+ * equal sum(num_new) (the host knows it; it sizes the outputs). */
+AS_API int as_pack_prefill(const int32_t* block_tables, int64_t bt_stride, const int32_t* row_ids,
+                    const int32_t* num_cached, const int32_t* num_new, int32_t num_seqs,
+                    int32_t total_new, int32_t max_blocks, int32_t block_size,
+                    int32_t* cu_seqlens_q, int64_t* positions, int64_t* slot_mapping,
+                    int32_t* seq_lens_k, int32_t* packed_bt, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (2) Fused RoPE + reshape_and_cache                                        */
+/* ------------------------------------------------------------------------- */
+
+/* For T tokens: rotate q [T, H, D] in place (row stride q_stride elements),
+ * rotate k [T, Kh, D] and write it to k_cache at slot_mapping[t]; write v
+ * unrotated to v_cache.  Rotate-half RoPE in fp32 from the fp32 table
+ * cos_sin [table_len, D] (first half cos, second half sin; llama.py:63-77),
+ * out = [x1*c - x2*s, x2*c + x1*s] rounded to the element type (llama.py:97-99).
+ * A negative slot skips that token's cache write.  k_out (optional, may be NULL)
+ * receives the rotated k [T, Kh, D] contiguous.  With cos_sin == NULL nothing is
+ * rotated: k and v are copied to their slots as given (write_kv_prefill /
+ * write_kv_decode, cache.py:125-156) and q / positions may be NULL. */
+AS_API int as_rope_reshape_and_cache(void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                              const void* v, int64_t v_stride, const int64_t* positions,
+                              const int64_t* slot_mapping, const float* cos_sin,
+                              int32_t table_len, void* k_cache, void* v_cache,
+                              int64_t num_slots, void* k_out, int32_t num_tokens,
+                              int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                              int32_t dtype, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (3) Paged GQA split-K decode attention                                    */
+/* ------------------------------------------------------------------------- */
+
+/* Bytes of workspace needed by as_paged_decode_attention. */
+AS_API size_t as_paged_decode_workspace_size(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                      int32_t head_dim, int32_t max_blocks,
+                                      int32_t blocks_per_split);
+
+/* One query token per sequence: out[b, h, :] = softmax(scale * q[b,h] . K^T) V over
+ * the seq_lens_k[b] keys of sequence b, read in place from the paged pool through
+ * block_tables [B, bt_stride] (KV head of query head h is h / (H/Kh)).
+ * q: [B, H, D] with row stride q_stride elements between tokens; out: [B, H*D] in
+ * out_layout (AS_LAYOUT_HEAD_MAJOR or AS_LAYOUT_DIM_MAJOR).
+ * blocks_per_split (>0) sets the split-K chunk; a sequence of n blocks uses
+ * ceil(n / blocks_per_split) CTAs per KV head, combined in-kernel by the last CTA.
+ * Workspace (as_paged_decode_workspace_size bytes, 256-byte aligned; needed when a
+ * sequence can span more than one split): its first round_up(B*H*4, 256) bytes are
+ * per-(sequence, head) arrival counters that must be zero when the call starts, and
+ * the call leaves them zero; the bytes after them hold split partials and need no
+ * initialisation.  Calls sharing a workspace must be stream-ordered. */
+AS_API int as_paged_decode_attention(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                              const void* v_cache, const int32_t* block_tables,
+                              int64_t bt_stride, const int32_t* seq_lens_k, int32_t num_seqs,
+                              int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                              int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                              float scale, int32_t blocks_per_split, void* workspace,
+                              size_t workspace_bytes, int32_t out_layout, int32_t dtype,
+                              as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (4) Varlen prefill attention over cached prefix blocks + new tokens       */
+/* ------------------------------------------------------------------------- */
+
+/* q: [total_q, H, D] (row stride q_stride elements), new tokens of sequence r at
+ * rows cu_seqlens_q[r] .. cu_seqlens_q[r+1]-1.  Keys/values: the first
+ * seq_lens_k[r] tokens of the sequence in the paged pool (prefix + new tokens,
+ * already written by as_rope_reshape_and_cache).  New token i of sequence r sits
+ * at position P + i with P = seq_lens_k[r] - num_new[r]; it attends to keys
+ * 0..P+i (cached prefix unmasked, new tokens causal: llama.py:171-180).
+ * out: [total_q, H*D]. */
+AS_API int as_varlen_prefill_attention(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                                const void* v_cache, const int32_t* block_tables,
+                                int64_t bt_stride, const int32_t* cu_seqlens_q,
+                                const int32_t* seq_lens_k, int32_t num_seqs,
+                                int32_t max_seqlen_q, int32_t total_q, int32_t num_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                int32_t num_blocks, int32_t max_blocks, float scale,
+                                int32_t dtype, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (5) Block gather / copy (prefix-cache seeding, gather_kv)                 */
+/* ------------------------------------------------------------------------- */
+
+/* For each plane p < num_planes and i < n:
+ *   copy bytes_per_block bytes from src + p*src_plane_stride + src_ids[i]*bytes_per_block
+ *                               to dst + p*dst_plane_stride + dst_ids[i]*bytes_per_block
+ * (dst_ids NULL means dst block i).  A plane is one (K|V, layer) slice of a pool;
+ * with dst_ids NULL and a dense dst this is gather_kv for all layers at once.
+ * bytes_per_block and both plane strides must be multiples of 16; src and dst
+ * 16-byte aligned.  src_num_blocks / dst_num_blocks bound the ids. */
+AS_API int as_block_copy(void* dst, const void* src, const int32_t* src_ids, const int32_t* dst_ids,
+                  int32_t n, int64_t bytes_per_block, int32_t num_planes,
+                  int64_t src_plane_stride, int64_t dst_plane_stride, int32_t src_num_blocks,
+                  int32_t dst_num_blocks, as_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AGENTSERVE_B200_H_ */

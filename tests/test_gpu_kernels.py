@@ -1,0 +1,331 @@
+"""Parity of every kernel with the oracle, through the C-ABI (ctypes) on a B200.
+
+Bars (from the task's parity contract):
+  packing / slot mapping / pool bytes / block copies: bit-exact;
+  RoPE (q in place, k into the pool): bit-exact with the reference's fp32 rotate-half;
+  attention: fp32 kernel vs fp32 oracle within 1e-5 abs; bf16/fp16 kernel vs fp32
+  oracle (on the same bf16/fp16-rounded inputs) within 2e-2 abs.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from agentserve_b200 import _native as N
+from agentserve_b200 import ops
+from oracle import attention as OA
+from oracle import paged as OP
+from oracle import rope as OR
+from tests.golden import scenarios as S
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+ATOL_FP32 = 1e-5
+ATOL_LOWP = 2e-2
+
+
+def make_tables(lens, num_blocks, g, extra_blocks=0):
+    """Block lists (from a random permutation of the pool) holding lens[i] tokens."""
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    tables, off = [], 0
+    for L in lens:
+        n = (L + 15) // 16 + extra_blocks
+        tables.append(perm[off:off + n])
+        off += n
+    assert off <= num_blocks
+    return tables
+
+
+def padded(tables, width=None):
+    w = width or max(len(t) for t in tables)
+    out = torch.zeros(len(tables), w, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        out[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    return out
+
+
+def status_ok():
+    bits = ops.device_status(clear=True)
+    assert bits == 0, f"device status bits {bits}"
+
+
+# ---------------------------------------------------------------- packing
+def test_pack_decode_bit_exact():
+    g = torch.Generator().manual_seed(1)
+    lens = [0, 1, 15, 16, 17, 31, 32, 33, 1000, 4095]
+    tables = make_tables([L + 1 for L in lens], 2048, g)
+    rows = torch.randperm(len(lens) + 5, generator=g)[:len(lens)]
+    table_dev = torch.zeros(len(lens) + 5, 300, dtype=torch.int32)
+    for i, r in enumerate(rows.tolist()):
+        table_dev[r, :len(tables[i])] = torch.tensor(tables[i], dtype=torch.int32)
+    pk = ops.pack_decode(table_dev.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV),
+                         rows.to(torch.int32).to(DEV), max_blocks=260)
+    pos, slots, lk, cu = OP.pack_decode(tables, lens)
+    assert pk.positions.cpu().numpy().tolist() == pos.tolist()
+    assert pk.slot_mapping.cpu().numpy().tolist() == slots.tolist()
+    assert pk.seq_lens_k.cpu().numpy().tolist() == lk.tolist()
+    assert pk.cu_seqlens_q.cpu().numpy().tolist() == cu.tolist()
+    assert torch.equal(pk.block_tables.cpu(), table_dev[rows][:, :260])
+    status_ok()
+
+
+def test_pack_prefill_bit_exact():
+    g = torch.Generator().manual_seed(2)
+    num_cached = [0, 32, 37, 0, 14336]
+    num_new = [5, 1, 64, 0, 600]
+    tables = make_tables([c + n for c, n in zip(num_cached, num_new)], 4096, g)
+    bt = padded(tables, 1000)
+    total = sum(num_new)
+    pk = ops.pack_prefill(bt.to(DEV), torch.tensor(num_cached, dtype=torch.int32, device=DEV),
+                          torch.tensor(num_new, dtype=torch.int32, device=DEV), total)
+    cu, pos, slots, lk = OP.pack_prefill(tables, num_cached, num_new)
+    assert pk.cu_seqlens_q.cpu().tolist() == cu.tolist()
+    assert pk.positions.cpu().tolist() == pos.tolist()
+    assert pk.slot_mapping.cpu().tolist() == slots.tolist()
+    assert pk.seq_lens_k.cpu().tolist() == lk.tolist()
+    status_ok()
+
+
+# ---------------------------------------------------------------- RoPE + cache
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,Kh,D", [(32, 8, 64), (32, 8, 128), (4, 2, 16)])
+def test_rope_reshape_and_cache_bit_exact(dtype, H, Kh, D):
+    g = torch.Generator().manual_seed(3)
+    T, NB = 37, 64
+    table = OR.precompute_rope_freqs(D, 4096, 500000.0)
+    fused = torch.randn(T, (H + 2 * Kh) * D, generator=g).to(dtype)
+    positions = torch.randint(0, 4096, (T,), generator=g)
+    slots = torch.randperm(NB * 16, generator=g)[:T]
+    slots[5] = -1  # padding token: no cache write
+    q, k, v = (fused[:, :H * D].view(T, H, D), fused[:, H * D:(H + Kh) * D].view(T, Kh, D),
+               fused[:, (H + Kh) * D:].view(T, Kh, D))
+    q_ref = OR.apply_rope(q.clone(), table[positions])
+    k_ref = OR.apply_rope(k.clone(), table[positions])
+    kc_ref = torch.zeros(NB * 16, Kh, D, dtype=dtype)
+    vc_ref = torch.zeros(NB * 16, Kh, D, dtype=dtype)
+    keep = slots >= 0
+    kc_ref[slots[keep]] = k_ref[keep]
+    vc_ref[slots[keep]] = v[keep]
+
+    fd = fused.to(DEV)
+    qd = fd[:, :H * D].view(T, H, D)
+    kd = fd[:, H * D:(H + Kh) * D].view(T, Kh, D)
+    vd = fd[:, (H + Kh) * D:].view(T, Kh, D)
+    kc = torch.zeros(NB, 16, Kh, D, dtype=dtype, device=DEV)
+    vc = torch.zeros_like(kc)
+    k_out = torch.empty(T, Kh, D, dtype=dtype, device=DEV)
+    ops.rope_reshape_and_cache(qd, kd, vd, positions.to(DEV), slots.to(DEV), table.to(DEV), kc,
+                               vc, k_out=k_out)
+    torch.cuda.synchronize()
+    assert torch.equal(qd.cpu(), q_ref), "q rotation not bit-exact"
+    assert torch.equal(k_out.cpu(), k_ref)
+    assert torch.equal(kc.view(-1, Kh, D).cpu(), kc_ref)
+    assert torch.equal(vc.view(-1, Kh, D).cpu(), vc_ref)
+    status_ok()
+
+
+def test_reshape_and_cache_without_rotation():
+    g = torch.Generator().manual_seed(4)
+    T, Kh, D, NB = 21, 8, 64, 16
+    k = torch.randn(T, Kh, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, Kh, D, generator=g).to(torch.bfloat16)
+    tables = make_tables([T], NB, g)
+    kc = torch.zeros(NB, 16, Kh, D, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    OP.write_kv(kc, vc, tables[0], 0, k, v)
+    _, _, slots, _ = OP.pack_prefill(tables, [0], [T])
+    kd = torch.zeros(NB, 16, Kh, D, dtype=torch.bfloat16, device=DEV)
+    vd = torch.zeros_like(kd)
+    ops.rope_reshape_and_cache(None, k.to(DEV), v.to(DEV), None,
+                               torch.from_numpy(slots).to(DEV), None, kd, vd)
+    assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
+    status_ok()
+
+
+# ---------------------------------------------------------------- decode attention
+def decode_case(lens, H, Kh, D, dtype, seed, NB=None):
+    g = torch.Generator().manual_seed(seed)
+    NB = NB or sum((L + 15) // 16 for L in lens) + 8
+    tables = make_tables(lens, NB, g)
+    kp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype)
+    vp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype)
+    q = torch.randn(len(lens), H, D, generator=g).to(dtype)
+    return tables, kp, vp, q
+
+
+def run_decode(tables, kp, vp, q, lens, bps, layout=N.AS_LAYOUT_HEAD_MAJOR, ws=None):
+    B, H, D = q.shape
+    Kh = kp.shape[2]
+    bt = padded(tables).to(DEV)
+    if ws is None:
+        ws = ops.new_decode_workspace(B, H, Kh, D, bt.shape[1], bps, DEV)
+    out = ops.paged_decode_attention(q.to(DEV), kp.to(DEV), vp.to(DEV), bt,
+                                     torch.tensor(lens, dtype=torch.int32, device=DEV),
+                                     1.0 / math.sqrt(D), bps, ws, out_layout=layout)
+    torch.cuda.synchronize()
+    return out.cpu()
+
+
+def oracle_decode(tables, kp, vp, q, lens):
+    return OA.decode_attention_from_pool(q.float(), kp.float(), vp.float(), tables, lens)
+
+
+def test_decode_config1_fp32_matches_reference_golden(golden):
+    inp = S.decode_cfg1_inputs()
+    kp, vp = inp["kpool"].clone(), inp["vpool"].clone()
+    for b, L in enumerate(inp["lens"]):
+        OP.write_kv(kp, vp, inp["tables"][b], L, inp["kn"][b:b + 1], inp["vn"][b:b + 1])
+    lens = [L + 1 for L in inp["lens"]]
+    for bps in (8, 64):
+        out = run_decode(inp["tables"], kp, vp, inp["q"], lens, bps)
+        ref = torch.from_numpy(golden["cfg1_out"]).reshape(8, -1)
+        torch.testing.assert_close(out, ref, rtol=0, atol=ATOL_FP32)
+    status_ok()
+
+
+LENS = [1, 15, 16, 17, 100, 257, 1000, 2113, 4096, 33]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bps", [4, 16, 256])
+def test_decode_lowp_fast_path(dtype, D, bps):
+    H, Kh = 32, 8
+    tables, kp, vp, q = decode_case(LENS, H, Kh, D, dtype, seed=D + bps)
+    out = run_decode(tables, kp, vp, q, LENS, bps)
+    ref = oracle_decode(tables, kp, vp, q, LENS).reshape(len(LENS), -1)
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+@pytest.mark.parametrize("H,Kh,D,dtype", [(32, 32, 64, torch.bfloat16), (32, 16, 64, torch.bfloat16),
+                                          (8, 1, 128, torch.bfloat16), (4, 2, 16, torch.bfloat16),
+                                          (4, 2, 16, torch.float32), (32, 8, 64, torch.float32),
+                                          (32, 8, 128, torch.float32), (24, 8, 128, torch.float16),
+                                          (64, 4, 64, torch.bfloat16)])
+def test_decode_geometries(H, Kh, D, dtype):
+    lens = [1, 16, 17, 300, 1025]
+    tables, kp, vp, q = decode_case(lens, H, Kh, D, dtype, seed=H * Kh + D)
+    ref = oracle_decode(tables, kp, vp, q, lens).reshape(len(lens), -1)
+    atol = ATOL_FP32 if dtype == torch.float32 else ATOL_LOWP
+    for bps in (4, 128):
+        out = run_decode(tables, kp, vp, q, lens, bps)
+        torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
+    status_ok()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_dim_major_layout(dtype):
+    lens = [17, 600, 5]
+    H, Kh, D = 32, 8, 64
+    tables, kp, vp, q = decode_case(lens, H, Kh, D, dtype, seed=9)
+    out = run_decode(tables, kp, vp, q, lens, 8, layout=N.AS_LAYOUT_DIM_MAJOR)
+    ref = OA.flatten_decode_output(oracle_decode(tables, kp, vp, q, lens))
+    atol = ATOL_FP32 if dtype == torch.float32 else ATOL_LOWP
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
+    status_ok()
+
+
+def test_decode_workspace_shared_across_batch_sizes():
+    H, Kh, D = 32, 8, 64
+    ws = ops.DecodeWorkspace(H, Kh, D, DEV)
+    for i, lens in enumerate([[700, 3], [900] * 12, [1200, 50, 2000], [4000] * 20, [64]]):
+        tables, kp, vp, q = decode_case(lens, H, Kh, D, torch.bfloat16, seed=40 + i)
+        bt_w = max(len(t) for t in tables)
+        buf = ws.get(len(lens), bt_w, 8)
+        out = run_decode(tables, kp, vp, q, lens, 8, ws=buf)
+        ref = oracle_decode(tables, kp, vp, q, lens).reshape(len(lens), -1)
+        torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+def test_decode_bad_block_id_is_flagged_not_faulted():
+    lens = [40, 40]
+    tables, kp, vp, q = decode_case(lens, 32, 8, 64, torch.bfloat16, seed=5)
+    tables[1][1] = 10_000_000  # outside the pool: the kernel clamps and flags it
+    run_decode(tables, kp, vp, q, lens, 8)
+    bits = ops.device_status(clear=True)
+    assert bits & 1
+    assert ops.device_status(clear=True) == 0
+
+
+# ---------------------------------------------------------------- prefill attention
+def prefill_case(num_cached, num_new, H, Kh, D, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    lens = [c + n for c, n in zip(num_cached, num_new)]
+    NB = sum((L + 15) // 16 for L in lens) + 4
+    tables = make_tables(lens, NB, g)
+    kp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype)
+    vp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype)
+    q = torch.randn(sum(num_new), H, D, generator=g).to(dtype)
+    cu = np.concatenate([[0], np.cumsum(num_new)]).astype(np.int32)
+    return tables, kp, vp, q, cu, lens
+
+
+def run_prefill(tables, kp, vp, q, cu, lens):
+    D = q.shape[2]
+    bt = padded(tables).to(DEV)
+    num_new = np.diff(cu)
+    out = ops.varlen_prefill_attention(q.to(DEV), kp.to(DEV), vp.to(DEV), bt,
+                                       torch.from_numpy(cu).to(DEV),
+                                       torch.tensor(lens, dtype=torch.int32, device=DEV),
+                                       int(num_new.max()), 1.0 / math.sqrt(D))
+    torch.cuda.synchronize()
+    return out.cpu()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,Kh,D", [(32, 8, 64), (32, 8, 128), (4, 2, 16)])
+def test_prefill_vs_oracle(dtype, H, Kh, D):
+    num_cached = [0, 32, 37, 0, 160]
+    num_new = [1, 17, 64, 130, 200]
+    tables, kp, vp, q, cu, lens = prefill_case(num_cached, num_new, H, Kh, D, dtype, seed=D)
+    out = run_prefill(tables, kp, vp, q, cu, lens)
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    atol = ATOL_FP32 if dtype == torch.float32 else ATOL_LOWP
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
+    status_ok()
+
+
+def test_prefill_long_prefix_bf16():
+    """Config-4 shape: a 14,336-token cached prefix plus a 600-token suffix."""
+    tables, kp, vp, q, cu, lens = prefill_case([14336], [600], 32, 8, 64, torch.bfloat16, 77)
+    out = run_prefill(tables, kp, vp, q, cu, lens)
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+# ---------------------------------------------------------------- block copy
+def test_block_copy_gather_and_seed_bit_exact():
+    g = torch.Generator().manual_seed(6)
+    L, NB, Kh, D = 3, 40, 8, 64
+    pool = torch.randn(2, L, NB, 16, Kh, D, generator=g).to(torch.bfloat16)
+    ids = torch.randperm(NB, generator=g)[:7].to(torch.int32)
+    bpb = 16 * Kh * D * 2
+    pd = pool.to(DEV)
+    out = torch.empty(2, L, 7, 16, Kh, D, dtype=torch.bfloat16, device=DEV)
+    ops.block_copy(out, pd, ids.to(DEV), None, bpb, 2 * L, NB * bpb, 7 * bpb, NB, 7)
+    assert torch.equal(out.cpu(), pool[:, :, ids.long()])
+    # seed the same payload into other blocks and gather again (round trip)
+    dst_ids = torch.randperm(NB, generator=g)[:7].to(torch.int32)
+    src_ids = torch.arange(7, dtype=torch.int32, device=DEV)
+    ops.block_copy(pd, out, src_ids, dst_ids.to(DEV), bpb, 2 * L, 7 * bpb, NB * bpb, 7, NB)
+    assert torch.equal(pd[:, :, dst_ids.long()].cpu(), pool[:, :, ids.long()])
+    # gather_kv semantics for one layer, 100 tokens
+    k = OP.gather_kv(pool[0, 1], ids.tolist(), 100)
+    buf = torch.empty(2, 7, 16, Kh, D, dtype=torch.bfloat16, device=DEV)
+    ops.block_copy(buf, pool.to(DEV)[0, 1], ids.to(DEV), None, bpb, 2, L * NB * bpb, 7 * bpb, NB, 7)
+    assert torch.equal(buf[0].reshape(-1, Kh, D)[:100].cpu(), k)
+    status_ok()
+
+
+def test_block_copy_bad_id_flagged():
+    pool = torch.zeros(4, 16, 16, dtype=torch.bfloat16, device=DEV)
+    out = torch.empty_like(pool)
+    ops.block_copy(out, pool, torch.tensor([0, 9], dtype=torch.int32, device=DEV), None, 512, 1,
+                   0, 0, 4, 4)
+    assert ops.device_status(clear=True) & 1

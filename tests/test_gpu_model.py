@@ -1,0 +1,167 @@
+"""End-to-end parity of the drop-in model (B200LlamaModel) on a B200.
+
+* fp32 logits of forward / prefix-hit forward / forward_decode_batch /
+  forward_decode_paged against golden vectors produced by the reference itself;
+* greedy tokens identical to the oracle (the reference's algorithm, same dtype, same
+  GPU) for 256 decode steps on the Llama-3.2-1B architecture in fp32;
+* the CUDA-graph decode step produces the same tokens as the eager path (bf16).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, greedy
+from agentserve_b200.config import ModelConfig
+from oracle.model import OracleLlama
+from oracle.paged import OracleBlockAllocator
+from oracle.weights import init_weights_
+from tests.golden import scenarios as S
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def b200_model(cfg, dtype=torch.float32, fused=False):
+    m = B200LlamaModel(cfg, dtype=dtype, device=DEV, fused_projections=fused)
+    init_weights_(m, seed=0)
+    return m.eval()
+
+
+@pytest.mark.parametrize("tag", list(S.MODEL_CONFIGS))
+def test_model_matches_reference_golden(golden, tag):
+    cfg = ModelConfig(**S.MODEL_CONFIGS[tag])
+    m = b200_model(cfg)
+    sc = S.model_scenario(tag, cfg)
+    tol = dict(rtol=0, atol=2e-4)
+    lg, kv = m.forward(sc["prompt"])
+    np.testing.assert_allclose(lg.cpu().numpy(), golden[f"{tag}_prefill_logits"], **tol)
+    pre = [(k[:32].clone(), v[:32].clone()) for k, v in kv]
+    lg2, _ = m.forward(sc["prompt"][32:], kv_cache=pre, position_offset=32)
+    np.testing.assert_allclose(lg2.cpu().numpy(), golden[f"{tag}_prefix_logits"], **tol)
+
+    caches, last, pos = [], [], []
+    for p in sc["batch_prompts"]:
+        l0, kvp = m.forward(p)
+        caches.append(kvp)
+        last.append(int(l0[-1].argmax()))
+        pos.append(len(p))
+    for step in range(S.DECODE_STEPS):
+        lg, caches = m.forward_decode_batch(last, caches, pos)
+        np.testing.assert_allclose(lg.cpu().numpy(), golden[f"{tag}_batch_logits"][step], **tol)
+        last = [int(t) for t in lg.argmax(-1)]
+        assert last == golden[f"{tag}_batch_tokens"][step].tolist()
+        pos = [x + 1 for x in pos]
+
+    a = DeviceBlockAllocator(64, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                             dtype=torch.float32, device=DEV)
+    rids, last, lens = [], [], []
+    for i, p in enumerate(sc["batch_prompts"]):
+        rid = f"r{i}"
+        a.allocate(rid, a.blocks_needed(len(p) + S.DECODE_STEPS + 1))
+        l0, kvp = m.forward(p)
+        for li, (k, v) in enumerate(kvp):
+            a.write_kv_prefill(rid, li, k, v)
+        rids.append(rid)
+        last.append(int(l0[-1].argmax()))
+        lens.append(len(p))
+    for step in range(S.DECODE_STEPS):
+        lg, _ = m.forward_decode_paged(last, lens, lens, a, rids)
+        np.testing.assert_allclose(lg.cpu().numpy(), golden[f"{tag}_paged_logits"][step], **tol)
+        last = [int(t) for t in lg.argmax(-1)]
+        assert last == golden[f"{tag}_paged_tokens"][step].tolist()
+        lens = [x + 1 for x in lens]
+    # the device pool holds what the reference's allocator held (same block ids)
+    assert a.blocks_for("r0") == golden[f"{tag}_block_tables"][0][:len(a.blocks_for("r0"))].tolist()
+
+
+def _prefill_both(m, o, oa, a, prompts, extra):
+    last_m, last_o, lens = [], [], []
+    for i, p in enumerate(prompts):
+        rid = f"s{i}"
+        a.allocate(rid, a.blocks_needed(len(p) + extra))
+        oa.allocate(rid, oa.blocks_needed(len(p) + extra))
+        lm, kvm = m.forward(p)
+        lo, kvo = o.forward(p)
+        for li in range(len(kvm)):
+            a.write_kv_prefill(rid, li, *kvm[li])
+            oa.write_kv_prefill(rid, li, *kvo[li])
+        last_m.append(int(lm[-1].argmax()))
+        last_o.append(int(lo[-1].argmax()))
+        lens.append(len(p))
+    return last_m, last_o, lens
+
+
+@pytest.mark.slow
+def test_greedy_256_steps_identical_fp32_llama1b():
+    """Config-2 architecture (16 layers, 2048 hidden, 32/8/64, FFN 8192, vocab 128256)
+    in fp32: 4 sequences, 256 greedy steps, tokens identical to the oracle."""
+    cfg = ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=16, vocab_size=128256,
+                      max_seq_len=4096, rope_theta=500000.0, intermediate_size=8192)
+    m = b200_model(cfg, torch.float32, fused=False)
+    o = OracleLlama(cfg).to(DEV)
+    init_weights_(o, seed=0)
+    o.eval()
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,), generator=g).tolist() for n in (200, 37, 130, 301)]
+    steps = 256
+    a = DeviceBlockAllocator(256, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                             dtype=torch.float32, device=DEV)
+    oa = OracleBlockAllocator(256, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                              allocate_tensor=True, device=DEV)
+    last_m, last_o, lens = _prefill_both(m, o, oa, a, prompts, steps + 1)
+    assert last_m == last_o
+    rids = [f"s{i}" for i in range(len(prompts))]
+    for step in range(steps):
+        lm, _ = m.forward_decode_paged(last_m, lens, lens, a, rids)
+        lo, _ = o.forward_decode_paged(last_o, lens, lens, oa, rids)
+        last_m = greedy(lm).tolist()
+        last_o = greedy(lo).tolist()
+        if last_m != last_o:
+            top2 = torch.topk(lo.float(), 2, dim=-1).values
+            margin = (top2[:, 0] - top2[:, 1]).min().item()
+            pytest.fail(f"tokens diverge at step {step} (oracle top-2 margin {margin:.3g})")
+        lens = [x + 1 for x in lens]
+
+
+def test_decode_graph_matches_eager_bf16():
+    cfg = ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=2, vocab_size=1024,
+                      max_seq_len=4096, rope_theta=500000.0, intermediate_size=2048)
+    m = b200_model(cfg, torch.bfloat16, fused=True)
+    g = torch.Generator().manual_seed(7)
+    B = 6
+    lens0 = torch.randint(20, 700, (B,), generator=g).tolist()
+    steps = 5
+    a = DeviceBlockAllocator(512, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                             dtype=torch.bfloat16, device=DEV)
+    a.kv_pool.copy_(torch.randn(a.kv_pool.shape, generator=g).to(torch.bfloat16))
+    rids = [f"g{i}" for i in range(B)]
+    for r, L in zip(rids, lens0):
+        a.allocate(r, a.blocks_needed(L + steps + 2))
+    pool0 = a.kv_pool.clone()
+    tok0 = torch.randint(3, cfg.vocab_size, (B,), generator=g).tolist()
+    m.decode_blocks_per_split = 8  # same split-K decomposition as the graph below
+    # eager
+    last, lens, eager = list(tok0), list(lens0), []
+    for _ in range(steps):
+        lg, _ = m.forward_decode_paged(last, lens, lens, a, rids)
+        last = greedy(lg).tolist()
+        eager.append(last)
+        lens = [x + 1 for x in lens]
+    # graph (self-advancing)
+    a.kv_pool.copy_(pool0)
+    max_blocks = max(len(a.blocks_for(r)) for r in rids)
+    dg = DecodeGraph(m, a, B, max_blocks, blocks_per_split=8, advance=True)
+    dg.capture(tok0, lens0, a.rows_for(rids))
+    graphed = []
+    for _ in range(steps):
+        graphed.append(dg.replay().tolist())
+    assert graphed == eager

@@ -1,0 +1,126 @@
+"""Host-side logic of the boundary, CPU only: the device allocator's bookkeeping keeps
+the reference BlockAllocator semantics (agentserve/engine/cache.py:33-119, pinned by
+the reference's tests/test_cache.py), its block-table rows mirror the host lists, and
+the split-K helpers behave."""
+
+import pytest
+import torch
+
+from agentserve_b200 import ops
+from agentserve_b200.cache import DeviceBlockAllocator
+from oracle import paged
+
+
+@pytest.fixture
+def alloc():
+    return DeviceBlockAllocator(num_blocks=32, block_size=16, allocate_tensor=False,
+                                device="cpu", max_seqs=64)
+
+
+def test_allocation_counts(alloc):
+    assert alloc.num_free_blocks() == 32 and alloc.num_used_blocks() == 0
+    ids = alloc.allocate("r1", 4)
+    assert len(ids) == 4 and alloc.num_free_blocks() == 28
+    ids2 = alloc.allocate("r2", 4)
+    assert set(ids).isdisjoint(ids2)
+    alloc.free("r1")
+    alloc.free("nonexistent")
+    assert alloc.num_free_blocks() == 28
+    assert alloc.memory_usage() == pytest.approx(4 / 32)
+
+
+def test_exhaustion_and_recovery(alloc):
+    with pytest.raises(MemoryError):
+        alloc.allocate("r", 33)
+    assert len(alloc.allocate("r", 32)) == 32
+    alloc.free("r")
+    assert len(alloc.allocate("r2", 32)) == 32
+
+
+def test_churn_and_interleaving(alloc):
+    for i in range(20):
+        alloc.allocate(f"q{i}", 2)
+        alloc.free(f"q{i}")
+    assert alloc.num_free_blocks() == 32
+    for i in range(16):
+        alloc.allocate(f"x{i}", 1)
+    for i in range(8):
+        alloc.free(f"x{i}")
+    assert alloc.num_free_blocks() == 24
+    alloc.allocate("new", 8)
+    assert alloc.num_free_blocks() == 16
+
+
+def test_blocks_needed_and_blocks_for(alloc):
+    assert [alloc.blocks_needed(n) for n in (0, 1, 16, 17, 31, 32)] == [0, 1, 1, 2, 2, 2]
+    ids = alloc.allocate("a", 3)
+    assert alloc.blocks_for("a") == ids
+    alloc.free("a")
+    assert alloc.blocks_for("a") == []
+
+
+def test_same_free_order_as_reference_allocator():
+    """The FIFO free list hands out the same ids as the reference for the same calls."""
+    ours = DeviceBlockAllocator(32, allocate_tensor=False, device="cpu")
+    ref = paged.OracleBlockAllocator(32)
+    script = [("a", "A", 3), ("a", "B", 2), ("f", "A", 0), ("a", "C", 4), ("a", "B", 1),
+              ("f", "B", 0), ("a", "D", 7)]
+    for op, rid, n in script:
+        if op == "a":
+            assert ours.allocate(rid, n) == ref.allocate(rid, n)
+        else:
+            ours.free(rid)
+            ref.free(rid)
+    assert list(ours._free) == list(ref._free)
+
+
+def test_device_table_rows_mirror_host_lists(alloc):
+    alloc.allocate("a", 3)
+    alloc.allocate("b", 2)
+    alloc.allocate("a", 2)  # a request can grow
+    ra, rb = alloc.row_of("a"), alloc.row_of("b")
+    assert ra != rb
+    assert alloc.block_tables[ra, :5].tolist() == alloc.blocks_for("a")
+    assert alloc.block_tables[rb, :2].tolist() == alloc.blocks_for("b")
+    alloc.free("a")
+    alloc.allocate("c", 1)
+    assert alloc.row_of("c") != rb  # rows are recycled without clobbering live ones
+    assert alloc.block_tables[rb, :2].tolist() == alloc.blocks_for("b")
+
+
+def test_row_capacity_limits():
+    a = DeviceBlockAllocator(64, allocate_tensor=False, device="cpu", max_seqs=2,
+                             max_blocks_per_seq=4)
+    a.allocate("x", 4)
+    with pytest.raises(MemoryError):
+        a.allocate("x", 1)
+    a.allocate("y", 1)
+    with pytest.raises(MemoryError):
+        a.allocate("z", 1)
+
+
+def test_block_size_must_be_16():
+    with pytest.raises(ValueError):
+        DeviceBlockAllocator(8, block_size=4, allocate_tensor=False, device="cpu")
+
+
+def test_choose_blocks_per_split_ranges():
+    # config-2 shape: 64 sequences x 8 KV heads, ~132 blocks each
+    bps = ops.choose_blocks_per_split(64 * 132, 64, 8, 257)
+    assert 8 <= bps <= 256 and bps % 4 == 0
+    # one short sequence: never below 8 blocks
+    assert ops.choose_blocks_per_split(2, 1, 8, 2) >= 8
+    # long contexts, few sequences -> more, shorter splits (but bounded)
+    assert ops.choose_blocks_per_split(2048, 1, 8, 2048) <= 256
+
+
+def test_decode_workspace_zeroes_counters_only_when_they_grow():
+    ws = ops.DecodeWorkspace(32, 8, 64, "cpu")
+    b = ws.get(8, 64, 16)
+    b[1024:].fill_(7)  # partials of a B=8 call sit right after its 1 KB of counters
+    b2 = ws.get(64, 64, 16)  # counters now cover 8 KB: must be zeroed again
+    assert b2.data_ptr() == b.data_ptr() or b2.numel() > b.numel()
+    assert int(b2[:64 * 32 * 4].sum()) == 0
+    b2[64 * 32 * 4:].fill_(3)
+    b3 = ws.get(8, 64, 16)  # smaller counter region: already zero, no memset needed
+    assert int(b3[:8 * 32 * 4].sum()) == 0
