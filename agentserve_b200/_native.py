@@ -26,6 +26,8 @@ AS_DTYPE_BF16 = 2
 AS_LAYOUT_HEAD_MAJOR = 0
 AS_LAYOUT_DIM_MAJOR = 1
 
+AS_DECODE_NOALLOC_SCRATCH_BYTES = 8 << 20
+
 # Every exported entry point with its C signature (restype, argtypes).
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -46,6 +48,9 @@ SIGNATURES = {
     "as_paged_decode_attention": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32,
                                                  _I32, _I32, _I32, _I32, _I32, _F32, _I32, _P,
                                                  _SZ, _I32, _I32, _P]),
+    "as_paged_decode_attention_noalloc": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I64, _P,
+                                                         _I32, _I32, _I32, _I32, _I32, _I32,
+                                                         _I32, _F32, _I32, _I32, _I32, _P]),
     "as_varlen_prefill_attention": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I64, _P, _P, _I32,
                                                    _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                                                    _I32, _F32, _I32, _P]),

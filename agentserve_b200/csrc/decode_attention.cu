@@ -19,6 +19,8 @@
 // Generic path (fp32, or other head dims / group sizes): CUDA-core warps with
 //   the same online softmax, used for the fp32 parity configuration and the tiny
 //   test geometry.
+#include <mutex>
+
 #include "common.cuh"
 #include "host_util.h"
 
@@ -707,4 +709,89 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
           k_cache, v_cache, block_tables, bt_stride, seq_lens_k, B, H, Kh, D, num_blocks,
           max_blocks, scale, blocks_per_split, max_splits, os_h, os_d, ws, s);
   }
+}
+
+// ===========================================================================
+// Allocation-free variant: split-K scratch in a static device array.
+//
+// Some callers cannot call cudaMalloc or hand us a workspace: a host runtime
+// whose device memory is entirely owned by another allocator (for example a
+// framework caching allocator that reserved the GPU up front and has nothing to
+// lend), or a serving loop that must never reach cudaMalloc's implicit device
+// synchronisation.  They still own q, the pool and out, but have nowhere to get
+// split-K scratch from.  This entry point uses a fixed-size array that lives in
+// the library's own device memory instead (every GPU that loads the library
+// holds AS_DECODE_NOALLOC_SCRATCH_BYTES of it until the process exits).
+// ===========================================================================
+static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[AS_DECODE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+void* g_noalloc_scratch_ptr[kNoallocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device.  The first call on a
+// device resolves it (cudaGetSymbolAddress with that device current) and caches it;
+// in host code the array's name is only a host-side stand-in, never a device address.
+int noalloc_scratch_on_current_device(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(AS_ERR_CUDA, "as_paged_decode_attention_noalloc: no current device (%s)",
+                cudaGetErrorString(e));
+  if (!g_noalloc_scratch_ptr[dev]) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_scratch_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+      if (e != cudaSuccess || !p)
+        return fail(AS_ERR_CUDA,
+                    "as_paged_decode_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(e));
+      g_noalloc_scratch_ptr[dev] = p;
+    }
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return AS_OK;
+}
+}  // namespace
+
+extern "C" int as_paged_decode_attention_noalloc(
+    void* out, const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+    const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens_k, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t num_blocks, int32_t max_blocks, float scale, int32_t blocks_per_split,
+    int32_t out_layout, int32_t dtype, as_stream_t stream) {
+  if (num_seqs <= 0 || num_heads <= 0 || max_blocks <= 0 || blocks_per_split <= 0)
+    return as_paged_decode_attention(out, q, q_stride, k_cache, v_cache, block_tables,
+                                     bt_stride, seq_lens_k, num_seqs, num_heads, num_kv_heads,
+                                     head_dim, block_size, num_blocks, max_blocks, scale,
+                                     blocks_per_split, nullptr, 0, out_layout, dtype, stream);
+  const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
+  void* scratch = nullptr;
+  if (max_splits > 1) {
+    const size_t need = as_paged_decode_workspace_size(num_seqs, num_heads, num_kv_heads,
+                                                       head_dim, max_blocks, blocks_per_split);
+    if (need == 0 || need > size_t(AS_DECODE_NOALLOC_SCRATCH_BYTES))
+      return fail(AS_ERR_WORKSPACE,
+                  "as_paged_decode_attention_noalloc: this call needs %zu bytes of split-K "
+                  "scratch but the static array holds %zu; use fewer sequences, a larger "
+                  "blocks_per_split, or as_paged_decode_attention with your own workspace",
+                  need, size_t(AS_DECODE_NOALLOC_SCRATCH_BYTES));
+    int rc = noalloc_scratch_on_current_device(&scratch);
+    if (rc != AS_OK) return rc;
+    // The array keeps whatever the previous call left.  The arrival counters at its
+    // front must start at zero; a previous call with fewer sequences may have put
+    // split partials where this call's counters are, so clear them every time.
+    const size_t counter_bytes = (size_t(num_seqs) * num_heads * sizeof(int32_t) + 255) / 256 * 256;
+    cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess)
+      return fail(AS_ERR_CUDA, "as_paged_decode_attention_noalloc: clearing counters failed: %s",
+                  cudaGetErrorString(e));
+  }
+  return as_paged_decode_attention(out, q, q_stride, k_cache, v_cache, block_tables, bt_stride,
+                                   seq_lens_k, num_seqs, num_heads, num_kv_heads, head_dim,
+                                   block_size, num_blocks, max_blocks, scale, blocks_per_split,
+                                   scratch, scratch ? size_t(AS_DECODE_NOALLOC_SCRATCH_BYTES) : 0,
+                                   out_layout, dtype, stream);
 }

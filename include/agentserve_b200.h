@@ -157,6 +157,29 @@ AS_API int as_paged_decode_attention(void* out, const void* q, int64_t q_stride,
                               size_t workspace_bytes, int32_t out_layout, int32_t dtype,
                               as_stream_t stream);
 
+/* Same computation as as_paged_decode_attention, for callers that cannot allocate
+ * device memory (their GPU memory belongs to another allocator, or their serving loop
+ * must not reach cudaMalloc's implicit synchronisation) and so have no workspace to
+ * pass.  No counterpart in the reference: it has no native code and no workspace.
+ * The split-K scratch is a static array of AS_DECODE_NOALLOC_SCRATCH_BYTES inside the
+ * library, held by every GPU that loads the library until the process exits.  A call
+ * whose scratch need (as_paged_decode_workspace_size) exceeds that is rejected with
+ * AS_ERR_WORKSPACE.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) for that device; make that first call before any stream
+ * capture.  Each call clears the array's counter region with cudaMemsetAsync on
+ * `stream` and allocates nothing.  All calls on a device share the one array: calls
+ * whose executions overlap on the GPU (different streams, no ordering) race. */
+#define AS_DECODE_NOALLOC_SCRATCH_BYTES (8u << 20)
+AS_API int as_paged_decode_attention_noalloc(void* out, const void* q, int64_t q_stride,
+                                             const void* k_cache, const void* v_cache,
+                                             const int32_t* block_tables, int64_t bt_stride,
+                                             const int32_t* seq_lens_k, int32_t num_seqs,
+                                             int32_t num_heads, int32_t num_kv_heads,
+                                             int32_t head_dim, int32_t block_size,
+                                             int32_t num_blocks, int32_t max_blocks, float scale,
+                                             int32_t blocks_per_split, int32_t out_layout,
+                                             int32_t dtype, as_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* (4) Varlen prefill attention over cached prefix blocks + new tokens       */
 /* ------------------------------------------------------------------------- */
