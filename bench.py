@@ -335,6 +335,10 @@ def run_b200(args):
         torch.distributed.barrier()
     if rank == 0:
         traffic = load_traffic()
+        traffic_launch = None
+        if traffic:
+            traffic_launch = (traffic["dram_bytes_per_launch"] * abytes
+                              / traffic["algorithmic_bytes_captured"])
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -350,7 +354,7 @@ def run_b200(args):
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": abytes, "launch_ms": attn_ms,
-                         "traffic": (traffic or {}).get("dram_bytes_per_launch_scaled"),
+                         "traffic": traffic_launch,
                          "traffic_source": (traffic or {}).get("source")},
             "e2e": {"value": e2e_value, "unit": "tok/s", "api": "B200LlamaModel.forward_decode_paged"
                     "(host lists) + greedy + .cpu()",
