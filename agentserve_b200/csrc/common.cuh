@@ -98,22 +98,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(0x989680u)  // suspend-time hint (ns)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
-// Upper bound on try_wait rounds before a wait is declared stuck.  Each round
-// may suspend the thread for up to the hint above, so this is far beyond any
-// legitimate wait on a TMA load or an MMA commit (milliseconds at most).
-constexpr uint32_t kMaxWaitRounds = 1u << 22;
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// A wait on a TMA load or an MMA commit completes within microseconds; one that has
+// not completed after this long is declared stuck (the kernel then records it and
+// winds down instead of spinning forever).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Returns false (and flags the status word) if the wait ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  for (uint32_t i = 0; i < kMaxWaitRounds; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) break;
   }
   flag_status(status, kStatusWaitTimeout);
   return false;

@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--cpu-sample-seqs", type=int, default=8)
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--layers", type=int, default=16, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -194,6 +195,65 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def prefill_flops(num_cached, num_new, H, D):
+    """Algorithmic FLOPs of varlen prefill attention: QK^T and PV over the visible
+    (query, key) pairs only, 2 FLOPs per MAC: 4*H*D*sum(T*P + T(T+1)/2)."""
+    return sum(4 * H * D * (T * P + T * (T + 1) // 2) for P, T in zip(num_cached, num_new))
+
+
+def measure_prefill(dev, reps: int = 10):
+    """The prefix-cache workload's prefill shape (a 14,336-token cached prefix plus a
+    600-token suffix, Llama-3.2-1B attention geometry, bf16), as the reference runs it
+    (one request per call) and as a varlen batch of 8 such requests, on the varlen
+    prefill kernel alone; CUDA events around `reps` launches."""
+    from agentserve_b200 import ops
+    H, Kh, D = 32, 8, 64
+    res = {}
+    for tag, R in (("1x", 1), ("8x", 8)):
+        num_cached, num_new = [14336] * R, [600] * R
+        lens = [c + n for c, n in zip(num_cached, num_new)]
+        nb = [(L + 15) // 16 for L in lens]
+        NB = sum(nb)
+        g = torch.Generator(device=dev).manual_seed(5)
+        kp = torch.randn(NB, 16, Kh, D, device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        vp = torch.randn(NB, 16, Kh, D, device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        q = torch.randn(sum(num_new), H, D, device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        bt = torch.zeros(R, max(nb), dtype=torch.int32)
+        perm = torch.randperm(NB, generator=torch.Generator().manual_seed(6))
+        off = 0
+        for i, n in enumerate(nb):
+            bt[i, :n] = perm[off:off + n].to(torch.int32)
+            off += n
+        bt = bt.to(dev)
+        cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(num_new), 0).tolist()),
+                          dtype=torch.int32, device=dev)
+        lk = torch.tensor(lens, dtype=torch.int32, device=dev)
+        out = torch.empty(sum(num_new), H * D, device=dev, dtype=torch.bfloat16)
+        for _ in range(2):
+            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        fl = prefill_flops(num_cached, num_new, H, D)
+        res[tag] = {"ms": ms, "tflops": fl / (ms / 1e3) / 1e12, "flops": fl}
+    return res
+
+
+def measured_bf16_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except (OSError, ValueError, KeyError):
+            pass
+    return 1590.0, "fallback"
+
+
 # ------------------------------------------------------------------ main arms
 def run_reference(args):
     rank, _, world = dist_env()
@@ -329,6 +389,7 @@ def run_b200(args):
     abytes = decode_attention_bytes(lk, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, 2)
     achieved = abytes / (attn_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
+    pf = measure_prefill(dev) if not args.no_prefill else None
     bits = ops.device_status(clear=True)
 
     if world > 1:
@@ -360,6 +421,14 @@ def run_b200(args):
                     "(host lists) + greedy + .cpu()",
                     "h2d_bytes_per_step": 4 * B * 8, "d2h_bytes_per_step": B * 8},
             "gpu_launches": args.steps * (1 + 2 * cfg.n_layers),
+            "prefill": None if pf is None else {
+                "kernel": "varlen prefill attention, tcgen05 + TMEM (bf16, D=64, GQA 4)",
+                "shape": "prefix 14336 + 600 new tokens per request (prefix-cache workload)",
+                "roofline": {"bound": "tensor", "achieved": pf["8x"]["tflops"],
+                             "peak": measured_bf16_peak()[0], "unit": "TFLOP/s",
+                             "frac": pf["8x"]["tflops"] / measured_bf16_peak()[0],
+                             "peak_source": measured_bf16_peak()[1] + " bf16_tflops (burst)"},
+                "one_request": pf["1x"], "eight_requests": pf["8x"]},
             "clocks": clk, "device_status": bits,
         }
         if world == 1 and not args.no_cpu_baseline:

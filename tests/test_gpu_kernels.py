@@ -329,3 +329,41 @@ def test_block_copy_bad_id_flagged():
     ops.block_copy(out, pool, torch.tensor([0, 9], dtype=torch.int32, device=DEV), None, 512, 1,
                    0, 0, 4, 4)
     assert ops.device_status(clear=True) & 1
+
+
+# ---------------------------------------------------------------- tensor-core prefill edges
+@pytest.mark.parametrize("H,Kh", [(32, 8), (8, 8), (16, 8), (64, 8), (32, 2)])
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_tensor_core_geometries(H, Kh, D):
+    """bf16 prefill on the tcgen05 kernel: GQA groups 1..16, new-token counts around the
+    query-tile size (128/group tokens), prefixes that are not block- or tile-aligned."""
+    tq = 128 // (H // Kh)
+    num_new = [1, tq - 1, tq, tq + 1, 3 * tq + 5]
+    num_cached = [0, 37, 130, 1, 16]
+    tables, kp, vp, q, cu, lens = prefill_case(num_cached, num_new, H, Kh, D, torch.bfloat16,
+                                               seed=H * 7 + D)
+    out = run_prefill(tables, kp, vp, q, cu, lens)
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+def test_prefill_tensor_core_strided_q_and_many_sequences():
+    """q as a column slice of a fused QKV buffer (row stride > H*D), 9 sequences."""
+    g = torch.Generator().manual_seed(31)
+    H, Kh, D = 32, 8, 64
+    num_cached = [0, 16, 300, 5, 0, 1000, 77, 128, 2]
+    num_new = [40, 1, 200, 33, 129, 64, 7, 300, 31]
+    tables, kp, vp, _, cu, lens = prefill_case(num_cached, num_new, H, Kh, D, torch.bfloat16, 32)
+    T = int(cu[-1])
+    fused = torch.randn(T, (H + 2 * Kh) * D, generator=g).to(torch.bfloat16)
+    q = fused[:, :H * D].view(T, H, D)
+    bt = padded(tables).to(DEV)
+    fd = fused.to(DEV)
+    out = ops.varlen_prefill_attention(fd[:, :H * D].view(T, H, D), kp.to(DEV), vp.to(DEV), bt,
+                                       torch.from_numpy(cu).to(DEV),
+                                       torch.tensor(lens, dtype=torch.int32, device=DEV),
+                                       max(num_new), 1.0 / math.sqrt(D))
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
