@@ -54,6 +54,9 @@ SIGNATURES = {
     "as_varlen_prefill_attention": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I64, _P, _P, _I32,
                                                    _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                                                    _I32, _F32, _I32, _P]),
+    "as_rmsnorm": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _F32, _I32, _P]),
+    "as_add_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _F32, _I32, _P]),
+    "as_silu_mul": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P]),
     "as_block_copy": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _I64, _I32, _I32,
                                      _P]),
 }

@@ -150,17 +150,29 @@ class B200LlamaModel(nn.Module):
                     qkv[:, (H + Kh) * D:].view(n, Kh, D))
         return (a.q_proj(h).view(n, H, D), a.k_proj(h).view(n, Kh, D), a.v_proj(h).view(n, Kh, D))
 
-    def _mlp(self, layer: _Layer, x: torch.Tensor) -> torch.Tensor:
+    def _mlp(self, layer: _Layer, h: torch.Tensor) -> torch.Tensor:
+        """SwiGLU on the already-normalised h (llama.py:207-211)."""
         f = layer.ffn
-        h = layer.ffn_norm(x)
         if self.fused_projections:
-            gu = F.linear(h, f._gu_w)
-            i = gu.shape[1] // 2
-            return f.down_proj(F.silu(gu[:, :i]) * gu[:, i:])
+            return f.down_proj(ops.silu_mul(F.linear(h, f._gu_w)))
         return f.down_proj(F.silu(f.gate_proj(h)) * f.up_proj(h))
 
-    def _logits(self, x: torch.Tensor) -> torch.Tensor:
-        return self.lm_head(self.norm(x))
+    def _run_layers(self, x: torch.Tensor, attention) -> torch.Tensor:
+        """The decoder stack (llama.py:218-238) with the residual adds fused into the
+        next pre-norm: x is the embedding output (updated in place as the residual
+        stream); attention(li, layer, h) returns the attention output fed to o_proj.
+        Returns the final-norm output."""
+        L = len(self.layers)
+        h = ops.rmsnorm(x, self.layers[0].attn_norm.weight, self.layers[0].attn_norm.eps)
+        for li, layer in enumerate(self.layers):
+            a = layer.attn.o_proj(attention(li, layer, h))
+            h = ops.add_rmsnorm(x, a, layer.ffn_norm.weight, layer.ffn_norm.eps)
+            nxt = self.layers[li + 1].attn_norm if li + 1 < L else self.norm
+            h = ops.add_rmsnorm(x, self._mlp(layer, h), nxt.weight, nxt.eps)
+        return h
+
+    def _logits(self, h: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(h)
 
     def _workspace(self, B: int, max_blocks: int, bps: int) -> torch.Tensor:
         ws = self._workspaces.get(self.device)
@@ -197,21 +209,21 @@ class B200LlamaModel(nn.Module):
         cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
         lk = torch.tensor([total], dtype=torch.int32, device=dev)
         new_cache = []
-        for li, layer in enumerate(self.layers):
-            kbuf = torch.empty(nblk, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
-            vbuf = torch.empty_like(kbuf)
+
+        def attention(li, layer, h):
+            kbuf = torch.zeros(nblk, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
+            vbuf = torch.zeros_like(kbuf)
             kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
             if P:
                 kf[:P].copy_(kv_cache[li][0])
                 vf[:P].copy_(kv_cache[li][1])
-            h = layer.attn_norm(x)
             q, k, v = self._qkv(layer, h)
             ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
-            attn = ops.varlen_prefill_attention(q, kbuf, vbuf, bt, cu, lk, T, self.scale)
-            x = x + layer.attn.o_proj(attn)
-            x = x + self._mlp(layer, x)
             new_cache.append((kf[:total], vf[:total]))
-        return self._logits(x), new_cache
+            return ops.varlen_prefill_attention(q, kbuf, vbuf, bt, cu, lk, T, self.scale)
+
+        h = self._run_layers(x, attention)
+        return self._logits(h), new_cache
 
     # ------------------------------------------------------------------ decode (lists)
     @torch.inference_mode()
@@ -247,7 +259,7 @@ class B200LlamaModel(nn.Module):
         x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
         new = [[] for _ in range(B)]
         short = [b for b in range(B) if lens[b] < max_len]
-        for li, layer in enumerate(self.layers):
+        def attention(li, layer, h):
             kbuf = torch.zeros(total_blocks, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
             vbuf = torch.zeros_like(kbuf)
             kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
@@ -255,13 +267,10 @@ class B200LlamaModel(nn.Module):
                 s = starts[b] * BS
                 kf[s:s + lens[b]].copy_(kv_caches[b][li][0])
                 vf[s:s + lens[b]].copy_(kv_caches[b][li][1])
-            h = layer.attn_norm(x)
             q, k, v = self._qkv(layer, h)
             ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
             attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,
                                               out_layout=self.decode_layout)
-            x = x + layer.attn.o_proj(attn)
-            x = x + self._mlp(layer, x)
             if self.reference_compat and short:
                 idx = torch.tensor([slots_host[b] for b in short], device=dev)
                 kf[idx] = 0
@@ -269,7 +278,10 @@ class B200LlamaModel(nn.Module):
             for b in range(B):
                 s = starts[b] * BS
                 new[b].append((kf[s:s + lens[b] + 1], vf[s:s + lens[b] + 1]))
-        return self._logits(x), new
+            return attn
+
+        h = self._run_layers(x, attention)
+        return self._logits(h), new
 
     # ------------------------------------------------------------------ decode (paged)
     def _decode_core(self, tokens: torch.Tensor, seq_lens: torch.Tensor, row_ids: torch.Tensor,
@@ -282,17 +294,15 @@ class B200LlamaModel(nn.Module):
         pk = ops.pack_decode(allocator.block_tables, seq_lens, row_ids, max_blocks)
         pos = pk.positions if positions is None else positions
         ws = self._workspace(B, max_blocks, bps)
-        x = self.embed(tokens)
-        for li, layer in enumerate(self.layers):
-            h = layer.attn_norm(x)
+
+        def attention(li, layer, h):
             q, k, v = self._qkv(layer, h)
             kp, vp = allocator.k_plane(li), allocator.v_plane(li)
             ops.rope_reshape_and_cache(q, k, v, pos, pk.slot_mapping, self.rope_table, kp, vp)
-            attn = ops.paged_decode_attention(q, kp, vp, pk.block_tables, pk.seq_lens_k,
+            return ops.paged_decode_attention(q, kp, vp, pk.block_tables, pk.seq_lens_k,
                                               self.scale, bps, ws, out_layout=self.decode_layout)
-            x = x + layer.attn.o_proj(attn)
-            x = x + self._mlp(layer, x)
-        return self._logits(x)
+
+        return self._logits(self._run_layers(self.embed(tokens), attention))
 
     @torch.inference_mode()
     def forward_decode_paged(self, last_token_ids: List[int], seq_lens: List[int],

@@ -281,3 +281,47 @@ def block_copy(dst: torch.Tensor, src: torch.Tensor, src_ids: torch.Tensor,
         _ptr(dst), _ptr(src), _ptr(src_ids), _ptr(dst_ids), n, int(bytes_per_block),
         int(num_planes), int(src_plane_stride), int(dst_plane_stride), int(src_num_blocks),
         int(dst_num_blocks), _stream(dst.device)), "as_block_copy")
+
+
+# ---------------------------------------------------------------------------
+# fused elementwise stages of the decode step
+# ---------------------------------------------------------------------------
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm of the rows of x [rows, dim] (llama.py:39-56)."""
+    _cuda(x, weight, out)
+    assert x.is_contiguous() and weight.is_contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    rows, dim = x.shape[0], x.shape[-1]
+    N.check(N.load().as_rmsnorm(_ptr(out), _ptr(x), _ptr(weight), x.numel() // dim, dim,
+                                float(eps), dtype_code(x.dtype), _stream(x.device)), "as_rmsnorm")
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps: float,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x += delta in place (rounded to x.dtype), returns rmsnorm(x)."""
+    _cuda(x, delta, weight, out)
+    assert x.is_contiguous() and delta.is_contiguous() and delta.shape == x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    dim = x.shape[-1]
+    N.check(N.load().as_add_rmsnorm(_ptr(out), _ptr(x), _ptr(delta), _ptr(weight),
+                                    x.numel() // dim, dim, float(eps), dtype_code(x.dtype),
+                                    _stream(x.device)), "as_add_rmsnorm")
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """gate_up [rows, 2*I] -> silu(gate) * up [rows, I] (llama.py:207-211)."""
+    _cuda(gate_up, out)
+    assert gate_up.is_contiguous()
+    rows, two_i = gate_up.shape
+    inter = two_i // 2
+    if out is None:
+        out = torch.empty(rows, inter, dtype=gate_up.dtype, device=gate_up.device)
+    N.check(N.load().as_silu_mul(_ptr(out), _ptr(gate_up), rows, inter,
+                                 dtype_code(gate_up.dtype), _stream(gate_up.device)),
+            "as_silu_mul")
+    return out

@@ -420,7 +420,9 @@ def run_b200(args):
             "e2e": {"value": e2e_value, "unit": "tok/s", "api": "B200LlamaModel.forward_decode_paged"
                     "(host lists) + greedy + .cpu()",
                     "h2d_bytes_per_step": 4 * B * 8, "d2h_bytes_per_step": B * 8},
-            "gpu_launches": args.steps * (1 + 2 * cfg.n_layers),
+            # per step: pack + first RMSNorm + per layer (RoPE/cache, attention,
+            # 2 x add+RMSNorm, SwiGLU)
+            "gpu_launches": args.steps * (2 + 5 * cfg.n_layers),
             "prefill": None if pf is None else {
                 "kernel": "varlen prefill attention, tcgen05 + TMEM (bf16, D=64, GQA 4)",
                 "shape": "prefix 14336 + 600 new tokens per request (prefix-cache workload)",

@@ -25,6 +25,8 @@
  *   as_varlen_prefill_attention llama.py:128-186 (prefill over cached prefix + new tokens)
  *   as_block_copy             cache.py:158-189 (gather_kv) and engine.py:274-281,338-345
  *                             (prefix-cache KV clone / seed)
+ *   as_rmsnorm / as_add_rmsnorm / as_silu_mul
+ *                             llama.py:39-56 (RMSNorm), :234-237 (residuals), :207-211 (SwiGLU)
  */
 #ifndef AGENTSERVE_B200_H_
 #define AGENTSERVE_B200_H_
@@ -215,6 +217,26 @@ AS_API int as_block_copy(void* dst, const void* src, const int32_t* src_ids, con
                   int32_t n, int64_t bytes_per_block, int32_t num_planes,
                   int64_t src_plane_stride, int64_t dst_plane_stride, int32_t src_num_blocks,
                   int32_t dst_num_blocks, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Fused elementwise stages of the decode step (rows x dim, contiguous rows)  */
+/* ------------------------------------------------------------------------- */
+
+/* out = to_T(x * rsqrt(mean(x^2) + eps)) * weight, statistics in fp32.
+ * Replaces RMSNorm.forward (llama.py:39-56). */
+AS_API int as_rmsnorm(void* out, const void* x, const void* weight, int64_t rows, int32_t dim,
+                      float eps, int32_t dtype, as_stream_t stream);
+
+/* x = to_T(x + delta) in place (the residual add, llama.py:234-237), then
+ * out = rmsnorm(x) as above: the residual add and the next pre-norm in one pass. */
+AS_API int as_add_rmsnorm(void* out, void* x, const void* delta, const void* weight,
+                          int64_t rows, int32_t dim, float eps, int32_t dtype,
+                          as_stream_t stream);
+
+/* gate_up [rows, 2*inter] = [gate | up]; out [rows, inter] = to_T(to_T(silu(gate)) * up).
+ * Replaces the SwiGLU activation of LlamaMLP.forward (llama.py:207-211). */
+AS_API int as_silu_mul(void* out, const void* gate_up, int64_t rows, int32_t inter,
+                       int32_t dtype, as_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -367,3 +367,38 @@ def test_prefill_tensor_core_strided_q_and_many_sequences():
     ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
     torch.testing.assert_close(out.float().cpu(), ref, rtol=0, atol=ATOL_LOWP)
     status_ok()
+
+
+# ---------------------------------------------------------------- fused norm / SwiGLU
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dim", [2048, 4096, 64, 3072])
+def test_rmsnorm_and_add_rmsnorm_match_reference_formula(dtype, dim):
+    from oracle.model import RMSNorm
+    g = torch.Generator().manual_seed(dim)
+    rows = 37
+    x = torch.randn(rows, dim, generator=g).to(dtype)
+    d = torch.randn(rows, dim, generator=g).to(dtype)
+    norm = RMSNorm(dim, 1e-5)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(dim, generator=g))
+    norm = norm.to(dtype)
+    ref = norm(x)
+    xs = (x + d)  # residual add rounded to dtype, as `x = x + h` in the reference
+    ref2 = norm(xs)
+    tol = dict(rtol=0, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
+    xd, dd, wd = x.to(DEV), d.to(DEV), norm.weight.detach().to(DEV)
+    out = ops.rmsnorm(xd, wd, 1e-5)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), **tol)
+    out2 = ops.add_rmsnorm(xd, dd, wd, 1e-5)
+    assert torch.equal(xd.cpu(), xs), "residual sum must be bit-exact"
+    torch.testing.assert_close(out2.cpu().float(), ref2.float(), **tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_silu_mul_matches_reference_formula(dtype):
+    g = torch.Generator().manual_seed(9)
+    gu = (3 * torch.randn(19, 2 * 8192, generator=g)).to(dtype)
+    ref = torch.nn.functional.silu(gu[:, :8192]) * gu[:, 8192:]
+    out = ops.silu_mul(gu.to(DEV))
+    tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), **tol)
