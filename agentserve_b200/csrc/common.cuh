@@ -152,6 +152,14 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       "l"(policy)
       : "memory");
 }
+// Bring a tile into L2 ahead of its shared-memory load (no smem, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int x, int y, int z,
+                                                   int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
 // L2 policies: KV blocks are streamed once per decode step -> evict first;
 // prefill K/V tiles are re-read by every query tile of the sequence -> evict last.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {

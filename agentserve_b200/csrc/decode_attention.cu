@@ -29,6 +29,19 @@ namespace {
 
 constexpr int kBlockSize = 16;
 constexpr int kMaxGroup = 8;
+constexpr int kMinAutoSplit = 32;  // smallest split chosen automatically (blocks_per_split 0)
+
+// blocks_per_split == 0: about three waves of CTAs over the SMs (4 fast-path CTAs fit
+// on an SM) for the largest possible batch (every sequence at max_blocks), never below
+// kMinAutoSplit blocks per CTA.  Shorter splits cost a partial merge; longer ones
+// leave SMs idle at the tail.
+inline int auto_blocks_per_split(int B, int Kh, int max_blocks, bool fast) {
+  const int64_t slots = int64_t(sm_count()) * (fast ? 4 : 8);
+  int64_t bps = (int64_t(B) * Kh * max_blocks + 3 * slots - 1) / (3 * slots);
+  if (bps < kMinAutoSplit) bps = kMinAutoSplit;
+  if (bps > 256) bps = 256;
+  return int(bps);
+}
 
 // ---------------------------------------------------------------------------
 // Workspace layout for split-K partials.
@@ -104,19 +117,141 @@ __device__ void splitk_finish(const DecodeWorkspace& ws, T* __restrict__ out, in
   if (threadIdx.x == 0) ws.counters[b * Kh + g] = 0;  // ready for the next call
 }
 
+// Fold n <= G paged blocks of one sequence at once (G independent S^T accumulator
+// chains for instruction-level parallelism).  Block k's K/V tiles are at kb[k]/vb[k]
+// and its first token at tok0 + k*tok_step.  The running max is lazy: scores are
+// exponentiated against the current max m_run unless some score exceeds it by more
+// than 2^8 (one warp vote); only then is the max reduced across the 8 lanes that
+// share a head column and O, l rescaled.  p stays <= 256, well inside bf16/fp32
+// range, and l, O, m stay mutually consistent, so the result is unchanged.
+constexpr float kLazyMaxSlack = 8.0f;  // log2 units
+
+template <typename T, int D, int G>
+__device__ __forceinline__ void fold_blocks(const uint32_t (&kb)[G], const uint32_t (&vb)[G], int n,
+                                            const uint32_t (&qb)[D / 16][2], int tok0,
+                                            int tok_step, int seq_len, float scale_log2,
+                                            float (&m_run)[2], float (&l_run)[2],
+                                            float (&o_acc)[D / 16][4], int lane,
+                                            uint32_t sub_bytes) {
+  constexpr int KT = D / 16;
+  float sc[G][4];
+#pragma unroll
+  for (int k = 0; k < G; ++k) sc[k][0] = sc[k][1] = sc[k][2] = sc[k][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < KT; ++kk) {
+    const int mi = lane >> 3;
+    const int row = (lane & 7) + 8 * (mi & 1);
+    const int chunk = 2 * (kk & 3) + (mi >> 1);
+    const uint32_t off = (kk >> 2) * sub_bytes + row * 128 + ((chunk ^ (row & 7)) << 4);
+#pragma unroll
+    for (int k = 0; k < G; ++k) {
+      if (k < n) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(kb[k] + off, a0, a1, a2, a3);
+        mma_16816<T>(sc[k], a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+    }
+  }
+  const int gq = lane >> 2;
+  float lm0 = -INFINITY, lm1 = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    const int t = tok0 + k * tok_step + gq;
+    const bool v0 = k < n && t < seq_len;
+    const bool v1 = k < n && t + 8 < seq_len;
+    sc[k][0] = v0 ? sc[k][0] * scale_log2 : -INFINITY;
+    sc[k][1] = v0 ? sc[k][1] * scale_log2 : -INFINITY;
+    sc[k][2] = v1 ? sc[k][2] * scale_log2 : -INFINITY;
+    sc[k][3] = v1 ? sc[k][3] * scale_log2 : -INFINITY;
+    lm0 = fmaxf(lm0, fmaxf(sc[k][0], sc[k][2]));
+    lm1 = fmaxf(lm1, fmaxf(sc[k][1], sc[k][3]));
+  }
+  const bool grow = lm0 > m_run[0] + kLazyMaxSlack || lm1 > m_run[1] + kLazyMaxSlack;
+  if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      lm0 = fmaxf(lm0, __shfl_xor_sync(0xffffffffu, lm0, o));
+      lm1 = fmaxf(lm1, __shfl_xor_sync(0xffffffffu, lm1, o));
+    }
+    const float mn0 = fmaxf(m_run[0], lm0), mn1 = fmaxf(m_run[1], lm1);
+    const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
+    m_run[0] = mn0;
+    m_run[1] = mn1;
+    l_run[0] *= al0;
+    l_run[1] *= al1;
+#pragma unroll
+    for (int mt = 0; mt < KT; ++mt) {
+      o_acc[mt][0] *= al0;
+      o_acc[mt][1] *= al1;
+      o_acc[mt][2] *= al0;
+      o_acc[mt][3] *= al1;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    if (k < n) {
+      const float p0 = fast_exp2(sc[k][0] - m_run[0]), p1 = fast_exp2(sc[k][1] - m_run[1]);
+      const float p2 = fast_exp2(sc[k][2] - m_run[0]), p3 = fast_exp2(sc[k][3] - m_run[1]);
+      l_run[0] += p0 + p2;
+      l_run[1] += p1 + p3;
+      const uint32_t pb0 = movmatrix_trans(pack2<T>(p0, p1));
+      const uint32_t pb1 = movmatrix_trans(pack2<T>(p2, p3));
+#pragma unroll
+      for (int mt = 0; mt < KT; ++mt) {
+        const int mi = lane >> 3;
+        const int row = (lane & 7) + 8 * (mi >> 1);
+        const int chunk = 2 * (mt & 3) + (mi & 1);
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(vb[k] + (mt >> 2) * sub_bytes + row * 128 + ((chunk ^ (row & 7)) << 4),
+                          a0, a1, a2, a3);
+        mma_16816<T>(o_acc[mt], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+  }
+}
+
+// Q^T of the GQA group of KV head g as B-fragments of S^T = K Q^T: column n = query
+// head g*group + n (zero columns past the group).
+template <typename T, int D>
+__device__ __forceinline__ void load_q_frags(uint32_t (&qb)[D / 16][2], const T* __restrict__ q,
+                                             int64_t q_stride, int b, int g, int group, int lane) {
+  const int gq = lane >> 2, tq = lane & 3;
+  const bool has_head = gq < group;
+  const T* qrow = q + int64_t(b) * q_stride + int64_t(g * group + (has_head ? gq : 0)) * D;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    qb[kk][0] = has_head ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * tq) : 0u;
+    qb[kk][1] = has_head ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * tq + 8) : 0u;
+  }
+}
+
 // ===========================================================================
 // Fast path: TMA + mma.sync, bf16/fp16, D in {64, 128}
 // ===========================================================================
+#ifndef AS_DECODE_SPLIT_WARPS
+#define AS_DECODE_SPLIT_WARPS 4
+#endif
+#ifndef AS_DECODE_SPLIT_STAGES_D64
+#define AS_DECODE_SPLIT_STAGES_D64 3
+#endif
+#ifndef AS_DECODE_SPLIT_STAGES_D128
+#define AS_DECODE_SPLIT_STAGES_D128 2
+#endif
+#ifndef AS_DECODE_SPLIT_FOLD
+#define AS_DECODE_SPLIT_FOLD 1
+#endif
+
 template <int D>
 struct FastCfg {
-  static constexpr int kConsumerWarps = 4;
+  static constexpr int kConsumerWarps = AS_DECODE_SPLIT_WARPS;
+  static constexpr int kFold = AS_DECODE_SPLIT_FOLD;  // blocks a warp folds per stage
   static constexpr int kThreads = (kConsumerWarps + 1) * 32;
   static constexpr int kSubTiles = D / 64;                 // 128-byte-wide swizzle sub-tiles
   static constexpr int kSubTileBytes = kBlockSize * 128;   // 16 rows x 128 B
   static constexpr int kTileBytes = kSubTiles * kSubTileBytes;  // one block, one head, K or V
   static constexpr int kSlotBytes = 2 * kTileBytes;        // K + V
-  static constexpr int kStageBytes = kConsumerWarps * kSlotBytes;
-  static constexpr int kStages = D == 64 ? 6 : 3;
+  static constexpr int kStageBytes = kConsumerWarps * kFold * kSlotBytes;
+  static constexpr int kStages = D == 64 ? AS_DECODE_SPLIT_STAGES_D64 : AS_DECODE_SPLIT_STAGES_D128;
   static constexpr int kMaxBlocksPerSplit = 256;
   static constexpr int kSmemBytes =
       1024 /*alignment slack*/ + kStages * kStageBytes + 2 * kStages * 8 +
@@ -158,7 +293,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
   if (split >= nsplit) return;
   const int blk_begin = split * bps;
   const int blk_count = min(bps, nblk - blk_begin);
-  const int niter = (blk_count + Cfg::kConsumerWarps - 1) / Cfg::kConsumerWarps;
+  constexpr int kPerStage = Cfg::kConsumerWarps * Cfg::kFold;
+  const int niter = (blk_count + kPerStage - 1) / kPerStage;
 
   extern __shared__ uint8_t smem_raw[];
   // 128B-swizzled TMA tiles need 1024-byte alignment in the shared window.
@@ -202,11 +338,11 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
         if (it >= NS) {
           if (!mbar_wait(&empty_bar[st], ((it / NS) + 1) & 1, status)) break;
         }
-        const int nb = min(Cfg::kConsumerWarps, blk_count - it * Cfg::kConsumerWarps);
+        const int nb = min(kPerStage, blk_count - it * kPerStage);
         mbar_arrive_expect_tx(&full_bar[st], uint32_t(nb * Cfg::kSlotBytes));
         uint8_t* stage = stages + st * Cfg::kStageBytes;
         for (int j = 0; j < nb; ++j) {
-          const int blk = s_blk[it * Cfg::kConsumerWarps + j];
+          const int blk = s_blk[it * kPerStage + j];
           uint8_t* slot = stage + j * Cfg::kSlotBytes;
 #pragma unroll
           for (int sub = 0; sub < Cfg::kSubTiles; ++sub) {
@@ -230,88 +366,28 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
   for (int i = 0; i < KT; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
 
   if (warp < Cfg::kConsumerWarps) {
-    // Q^T as the B operand of S^T = K Q^T: column n = query head g*group + n.
     uint32_t qb[KT][2];
-    {
-      const bool has_head = gq < group;
-      const T* qrow = q + int64_t(b) * q_stride + int64_t(g * group + (has_head ? gq : 0)) * D;
-#pragma unroll
-      for (int kk = 0; kk < KT; ++kk) {
-        qb[kk][0] = has_head ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * tq) : 0u;
-        qb[kk][1] =
-            has_head ? *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * tq + 8) : 0u;
-      }
-    }
+    load_q_frags<T, D>(qb, q, q_stride, b, g, group, lane);
 
     for (int it = 0; it < niter; ++it) {
       const int st = it % NS;
-      const int local = it * Cfg::kConsumerWarps + warp;
-      if (local < blk_count) {
+      const int local = it * kPerStage + warp * Cfg::kFold;  // this warp's first block
+      const int n = min(Cfg::kFold, blk_count - local);       // < 1 only in the last stage
+      if (n > 0) {
         if (!mbar_wait(&full_bar[st], (it / NS) & 1, status)) {
           timed_out = true;
           break;
         }
-        const uint32_t kbase =
-            smem_u32(stages + st * Cfg::kStageBytes + warp * Cfg::kSlotBytes);
-        const uint32_t vbase = kbase + Cfg::kTileBytes;
-
-        // S^T[16 tokens x 8 heads]
-        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t kb[Cfg::kFold], vb[Cfg::kFold];
 #pragma unroll
-        for (int kk = 0; kk < KT; ++kk) {
-          const int mi = lane >> 3;
-          const int row = (lane & 7) + 8 * (mi & 1);
-          const int chunk = 2 * (kk & 3) + (mi >> 1);
-          const uint32_t addr = kbase + (kk >> 2) * Cfg::kSubTileBytes + row * 128 +
-                                ((chunk ^ (row & 7)) << 4);
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4(addr, a0, a1, a2, a3);
-          mma_16816<T>(sacc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        for (int k = 0; k < Cfg::kFold; ++k) {
+          kb[k] = smem_u32(stages + st * Cfg::kStageBytes +
+                           (warp * Cfg::kFold + k) * Cfg::kSlotBytes);
+          vb[k] = kb[k] + Cfg::kTileBytes;
         }
-        // mask + scale (log2 units)
-        const int tok0 = (blk_begin + local) * kBlockSize + gq;
-        const bool v0 = tok0 < seq_len;
-        const bool v1 = tok0 + 8 < seq_len;
-        float s0 = v0 ? sacc[0] * scale_log2 : -INFINITY;
-        float s1 = v0 ? sacc[1] * scale_log2 : -INFINITY;
-        float s2 = v1 ? sacc[2] * scale_log2 : -INFINITY;
-        float s3 = v1 ? sacc[3] * scale_log2 : -INFINITY;
-        float bm0 = fmaxf(s0, s2), bm1 = fmaxf(s1, s3);
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, o));
-          bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, o));
-        }
-        const float mn0 = fmaxf(m_run[0], bm0), mn1 = fmaxf(m_run[1], bm1);
-        const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
-        m_run[0] = mn0;
-        m_run[1] = mn1;
-        const float p0 = fast_exp2(s0 - mn0), p1 = fast_exp2(s1 - mn1);
-        const float p2 = fast_exp2(s2 - mn0), p3 = fast_exp2(s3 - mn1);
-        l_run[0] = l_run[0] * al0 + p0 + p2;
-        l_run[1] = l_run[1] * al1 + p1 + p3;
-#pragma unroll
-        for (int mt = 0; mt < KT; ++mt) {
-          o_acc[mt][0] *= al0;
-          o_acc[mt][1] *= al1;
-          o_acc[mt][2] *= al0;
-          o_acc[mt][3] *= al1;
-        }
-        // P^T (tokens x heads) -> B fragments (k = tokens, n = heads)
-        const uint32_t pb0 = movmatrix_trans(pack2<T>(p0, p1));
-        const uint32_t pb1 = movmatrix_trans(pack2<T>(p2, p3));
-        // O^T[dims x heads] += V^T[dims x tokens] * P^T
-#pragma unroll
-        for (int mt = 0; mt < KT; ++mt) {
-          const int mi = lane >> 3;
-          const int row = (lane & 7) + 8 * (mi >> 1);
-          const int chunk = 2 * (mt & 3) + (mi & 1);
-          const uint32_t addr = vbase + (mt >> 2) * Cfg::kSubTileBytes + row * 128 +
-                                ((chunk ^ (row & 7)) << 4);
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4_trans(addr, a0, a1, a2, a3);
-          mma_16816<T>(o_acc[mt], a0, a1, a2, a3, pb0, pb1);
-        }
+        fold_blocks<T, D, Cfg::kFold>(kb, vb, n, qb, (blk_begin + local) * kBlockSize,
+                                      kBlockSize, seq_len, scale_log2, m_run, l_run, o_acc, lane,
+                                      Cfg::kSubTileBytes);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -615,8 +691,9 @@ extern "C" size_t as_paged_decode_workspace_size(int32_t num_seqs, int32_t num_h
                                                  int32_t num_kv_heads, int32_t head_dim,
                                                  int32_t max_blocks, int32_t blocks_per_split) {
   if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks <= 0 ||
-      blocks_per_split <= 0)
+      blocks_per_split < 0 || num_heads % num_kv_heads)
     return 0;
+  if (blocks_per_split == 0) blocks_per_split = kMinAutoSplit;  // covers every automatic choice
   const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
   // counters are per (sequence, query head) to cover both kernel variants
   return workspace_bytes(num_seqs, num_heads, num_heads, head_dim, max_splits);
@@ -638,7 +715,7 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
                 block_size);
   if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
       head_dim <= 0 || head_dim > 256 || num_blocks <= 0 || max_blocks <= 0 ||
-      bt_stride < max_blocks || blocks_per_split <= 0)
+      bt_stride < max_blocks || blocks_per_split < 0)
     return fail(AS_ERR_INVALID_ARG,
                 "as_paged_decode_attention: bad sizes (B=%d H=%d Kh=%d D=%d NB=%d maxb=%d bps=%d)",
                 num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, max_blocks,
@@ -649,12 +726,16 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
     return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: null pointer");
   if (q_stride < int64_t(num_heads) * head_dim)
     return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: q_stride < H*D");
-  const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
   const int group = num_heads / num_kv_heads;
   const bool fast = fast_path_ok(dtype, head_dim, group, q, q_stride, k_cache, v_cache);
+  if (blocks_per_split == 0)
+    blocks_per_split = auto_blocks_per_split(num_seqs, num_kv_heads, max_blocks, fast);
+  const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
   if (fast && blocks_per_split > FastCfg<64>::kMaxBlocksPerSplit)
     return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: blocks_per_split > %d",
                 FastCfg<64>::kMaxBlocksPerSplit);
+  if (out_layout != AS_LAYOUT_HEAD_MAJOR && out_layout != AS_LAYOUT_DIM_MAJOR)
+    return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: unknown out_layout %d", out_layout);
   DecodeWorkspace ws{nullptr, nullptr, nullptr, nullptr};
   if (max_splits > 1) {
     const size_t need = workspace_bytes(num_seqs, num_heads, num_heads, head_dim, max_splits);
@@ -762,14 +843,17 @@ extern "C" int as_paged_decode_attention_noalloc(
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
     int32_t num_blocks, int32_t max_blocks, float scale, int32_t blocks_per_split,
     int32_t out_layout, int32_t dtype, as_stream_t stream) {
-  if (num_seqs <= 0 || num_heads <= 0 || max_blocks <= 0 || blocks_per_split <= 0)
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || max_blocks <= 0 ||
+      blocks_per_split < 0)
     return as_paged_decode_attention(out, q, q_stride, k_cache, v_cache, block_tables,
                                      bt_stride, seq_lens_k, num_seqs, num_heads, num_kv_heads,
                                      head_dim, block_size, num_blocks, max_blocks, scale,
                                      blocks_per_split, nullptr, 0, out_layout, dtype, stream);
-  const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
+  // blocks_per_split == 0 (split chosen by the library) may use scratch
+  const bool uses_scratch =
+      blocks_per_split == 0 || (max_blocks + blocks_per_split - 1) / blocks_per_split > 1;
   void* scratch = nullptr;
-  if (max_splits > 1) {
+  if (uses_scratch) {
     const size_t need = as_paged_decode_workspace_size(num_seqs, num_heads, num_kv_heads,
                                                        head_dim, max_blocks, blocks_per_split);
     if (need == 0 || need > size_t(AS_DECODE_NOALLOC_SCRATCH_BYTES))

@@ -106,8 +106,9 @@ class B200LlamaModel(nn.Module):
         self.decode_layout = N.AS_LAYOUT_DIM_MAJOR if reference_compat else N.AS_LAYOUT_HEAD_MAJOR
         self._fused = False
         self._workspaces = {}
-        # split-K chunk (16-token blocks) for decode attention; None picks it per call
-        self.decode_blocks_per_split: Optional[int] = None
+        # decode attention work split: 0 = balanced persistent partition of all
+        # (sequence, KV head, block) units (default); > 0 = fixed split-K chunk in blocks
+        self.decode_blocks_per_split: int = 0
 
     @property
     def device(self) -> torch.device:
@@ -254,7 +255,7 @@ class B200LlamaModel(nn.Module):
         slots = torch.tensor(slots_host, dtype=torch.int64, device=dev)
         pos = torch.tensor(position_offsets, dtype=torch.int64, device=dev)
         lk = torch.tensor([L + 1 for L in lens], dtype=torch.int32, device=dev)
-        bps = ops.choose_blocks_per_split(total_blocks, B, self.Kh, mb)
+        bps = self.decode_blocks_per_split
         ws = self._workspace(B, mb, bps)
         x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
         new = [[] for _ in range(B)]
@@ -328,9 +329,6 @@ class B200LlamaModel(nn.Module):
         pos = None if list(position_offsets) == list(seq_lens) else d[3].contiguous()
         max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
         bps = self.decode_blocks_per_split
-        if bps is None:
-            total = sum((L + 1 + BS - 1) // BS for L in seq_lens)
-            bps = ops.choose_blocks_per_split(total, B, self.Kh, max_blocks)
         logits = self._decode_core(tokens, sl, rid, allocator, max_blocks, bps, positions=pos)
         return logits, None
 

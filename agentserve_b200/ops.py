@@ -202,19 +202,6 @@ class DecodeWorkspace:
         return self.buf
 
 
-def choose_blocks_per_split(total_blocks: int, num_seqs: int, num_kv_heads: int,
-                            max_blocks: int, num_sms: int = 148) -> int:
-    """Split-K chunk (in 16-token blocks) so that the CTAs of one call cover the SMs
-    a few times over: each CTA streams one chunk of one (sequence, KV head)."""
-    target_ctas = 4 * num_sms
-    pairs = max(1, num_seqs * num_kv_heads)
-    per_pair = max(1, total_blocks // max(1, num_seqs))
-    splits = max(1, -(-target_ctas // pairs))
-    bps = max(8, -(-per_pair // splits))
-    bps = min(bps, 256, max(8, max_blocks))
-    return int(-(-bps // 4) * 4)
-
-
 def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            block_tables: torch.Tensor, seq_lens_k: torch.Tensor, scale: float,
                            blocks_per_split: int, workspace: Optional[torch.Tensor],

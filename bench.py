@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--blocks-per-split", type=int, default=0)
     ap.add_argument("--layers", type=int, default=16, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -306,8 +307,7 @@ def run_b200(args):
         alloc.allocate(r, n)
     rows = alloc.rows_for(rids)
     max_blocks = max(nblk)
-    total_blocks = sum((L + 1 + 15) // 16 for L in lens)
-    bps = ops.choose_blocks_per_split(total_blocks, B, cfg.n_kv_heads, max_blocks)
+    bps = args.blocks_per_split  # 0: balanced persistent partition
     model.decode_blocks_per_split = bps
     tokens0 = torch.randint(3, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(7 + rank))
 

@@ -143,8 +143,9 @@ AS_API size_t as_paged_decode_workspace_size(int32_t num_seqs, int32_t num_heads
  * block_tables [B, bt_stride] (KV head of query head h is h / (H/Kh)).
  * q: [B, H, D] with row stride q_stride elements between tokens; out: [B, H*D] in
  * out_layout (AS_LAYOUT_HEAD_MAJOR or AS_LAYOUT_DIM_MAJOR).
- * blocks_per_split (>0) sets the split-K chunk; a sequence of n blocks uses
- * ceil(n / blocks_per_split) CTAs per KV head, combined in-kernel by the last CTA.
+ * blocks_per_split sets the split-K chunk (0: chosen by the library from B, Kh,
+ * max_blocks and the SM count); a sequence of n blocks uses ceil(n / blocks_per_split)
+ * CTAs per KV head, combined in-kernel by the last CTA.
  * Workspace (as_paged_decode_workspace_size bytes, 256-byte aligned; needed when a
  * sequence can span more than one split): its first round_up(B*H*4, 256) bytes are
  * per-(sequence, head) arrival counters that must be zero when the call starts, and

@@ -191,7 +191,7 @@ LENS = [1, 15, 16, 17, 100, 257, 1000, 2113, 4096, 33]
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("bps", [4, 16, 256])
+@pytest.mark.parametrize("bps", [0, 4, 16, 256])
 def test_decode_lowp_fast_path(dtype, D, bps):
     H, Kh = 32, 8
     tables, kp, vp, q = decode_case(LENS, H, Kh, D, dtype, seed=D + bps)
@@ -211,7 +211,7 @@ def test_decode_geometries(H, Kh, D, dtype):
     tables, kp, vp, q = decode_case(lens, H, Kh, D, dtype, seed=H * Kh + D)
     ref = oracle_decode(tables, kp, vp, q, lens).reshape(len(lens), -1)
     atol = ATOL_FP32 if dtype == torch.float32 else ATOL_LOWP
-    for bps in (4, 128):
+    for bps in (0, 4, 128):
         out = run_decode(tables, kp, vp, q, lens, bps)
         torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
     status_ok()
@@ -222,10 +222,11 @@ def test_decode_dim_major_layout(dtype):
     lens = [17, 600, 5]
     H, Kh, D = 32, 8, 64
     tables, kp, vp, q = decode_case(lens, H, Kh, D, dtype, seed=9)
-    out = run_decode(tables, kp, vp, q, lens, 8, layout=N.AS_LAYOUT_DIM_MAJOR)
     ref = OA.flatten_decode_output(oracle_decode(tables, kp, vp, q, lens))
     atol = ATOL_FP32 if dtype == torch.float32 else ATOL_LOWP
-    torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
+    for bps in (0, 8):
+        out = run_decode(tables, kp, vp, q, lens, bps, layout=N.AS_LAYOUT_DIM_MAJOR)
+        torch.testing.assert_close(out.float(), ref, rtol=0, atol=atol)
     status_ok()
 
 
@@ -235,10 +236,34 @@ def test_decode_workspace_shared_across_batch_sizes():
     for i, lens in enumerate([[700, 3], [900] * 12, [1200, 50, 2000], [4000] * 20, [64]]):
         tables, kp, vp, q = decode_case(lens, H, Kh, D, torch.bfloat16, seed=40 + i)
         bt_w = max(len(t) for t in tables)
-        buf = ws.get(len(lens), bt_w, 8)
-        out = run_decode(tables, kp, vp, q, lens, 8, ws=buf)
-        ref = oracle_decode(tables, kp, vp, q, lens).reshape(len(lens), -1)
-        torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+        for bps in (8, 0):
+            buf = ws.get(len(lens), bt_w, bps)
+            out = run_decode(tables, kp, vp, q, lens, bps, ws=buf)
+            ref = oracle_decode(tables, kp, vp, q, lens).reshape(len(lens), -1)
+            torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_decode_balanced_large_batch_with_empty_sequences(D):
+    """Balanced partition over 300 sequences of mixed lengths (1 .. 3000 tokens, some
+    empty: those get a zero row), run twice on one workspace."""
+    g = torch.Generator().manual_seed(D)
+    lens = torch.randint(1, 3000, (300,), generator=g).tolist()
+    for i in (0, 7, 150, 299):
+        lens[i] = 0
+    H, Kh = 32, 8
+    nz = [L for L in lens]
+    tables, kp, vp, q = decode_case([max(L, 1) for L in nz], H, Kh, D, torch.bfloat16, seed=D + 1)
+    ws = ops.new_decode_workspace(len(lens), H, Kh, D, max(len(t) for t in tables), 0, DEV)
+    for _ in range(2):
+        out = run_decode(tables, kp, vp, q, lens, 0, ws=ws)
+        nonempty = [i for i, L in enumerate(lens) if L > 0]
+        ref = oracle_decode([tables[i] for i in nonempty], kp, vp, q[nonempty],
+                            [lens[i] for i in nonempty]).reshape(len(nonempty), -1)
+        torch.testing.assert_close(out[nonempty].float(), ref, rtol=0, atol=ATOL_LOWP)
+        empty = [i for i, L in enumerate(lens) if L == 0]
+        assert torch.count_nonzero(out[empty]) == 0
     status_ok()
 
 

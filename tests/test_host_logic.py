@@ -104,16 +104,6 @@ def test_block_size_must_be_16():
         DeviceBlockAllocator(8, block_size=4, allocate_tensor=False, device="cpu")
 
 
-def test_choose_blocks_per_split_ranges():
-    # config-2 shape: 64 sequences x 8 KV heads, ~132 blocks each
-    bps = ops.choose_blocks_per_split(64 * 132, 64, 8, 257)
-    assert 8 <= bps <= 256 and bps % 4 == 0
-    # one short sequence: never below 8 blocks
-    assert ops.choose_blocks_per_split(2, 1, 8, 2) >= 8
-    # long contexts, few sequences -> more, shorter splits (but bounded)
-    assert ops.choose_blocks_per_split(2048, 1, 8, 2048) <= 256
-
-
 def test_decode_workspace_zeroes_counters_only_when_they_grow():
     ws = ops.DecodeWorkspace(32, 8, 64, "cpu")
     b = ws.get(8, 64, 16)
