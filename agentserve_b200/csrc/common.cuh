@@ -152,6 +152,16 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       "l"(policy)
       : "memory");
 }
+// 16-byte asynchronous global->shared copy (L2 only), and an arrive on an mbarrier
+// that fires when all of this thread's prior cp.async copies have landed (the
+// barrier's expected count includes these arrivals).
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 // Bring a tile into L2 ahead of its shared-memory load (no smem, no barrier).
 __device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int x, int y, int z,
                                                    int w) {

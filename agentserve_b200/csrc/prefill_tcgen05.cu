@@ -35,13 +35,18 @@ namespace asb {
 namespace {
 
 constexpr int kBS = 16;
+constexpr float kLazySlack = 8.0f;  // log2 units: rescale only when a row max grows > 2^8
+
+#ifndef AS_PREFILL_STAGES
+#define AS_PREFILL_STAGES 2
+#endif
 
 template <int D>
 struct PfCfg {
   static constexpr int kBM = 128;                 // Q-tile rows
   static constexpr int kBN = 128;                 // keys per KV tile (8 blocks)
   static constexpr int kSub = D / 64;             // 64-element (128 B) swizzle sub-tiles
-  static constexpr int kStages = 2;
+  static constexpr int kStages = AS_PREFILL_STAGES;
   static constexpr int kSubBytes = 128 * 128;     // 128 rows x 128 B
   static constexpr int kQBytes = kSub * kSubBytes;
   static constexpr int kKVBytes = kSub * kSubBytes;  // one of K or V for one KV tile
@@ -55,13 +60,13 @@ struct PfCfg {
   static constexpr int kSmemBytes = kOffBar + 256;
   static constexpr int kThreads = 192;
   static constexpr int kTmemCols = 256;
-  static constexpr int kMinBlocks = (D == 64) ? 2 : 1;
+  static constexpr int kMinBlocks = (kOffBar + 256) * 2 <= 225 * 1024 ? 2 : 1;
 };
 
 struct PfBars {
   uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
   uint64_t s_full;
   uint64_t s_free;
   uint64_t p_full;
@@ -173,7 +178,22 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kSubBytes, &tmap_q, &bars->q_full, s * 64,
                     g * group, q_begin + t0, pol_q);
     }
+    // K/V by TMA: lane b issues block b of the tile (K and V boxes of 16 tokens x 64
+    // columns of this KV head); block ids of tile j+1 are fetched while tile j issues.
+    auto load_id = [&](int jt) -> int {
+      const int blk = 8 * jt + (lane & 7);
+      int id = fill_ok;  // keys past the sequence: finite filler data, masked to p = 0
+      if (blk < nblk_seq) {
+        id = __ldg(bt + int64_t(r) * bt_stride + blk);
+        if (id < 0 || id >= num_blocks) {
+          flag_status(status, kStatusBadBlockId);
+          id = fill_ok;
+        }
+      }
+      return id;
+    };
     const uint64_t pol_kv = l2_policy_evict_last();
+    int id_next = load_id(0);
     for (int j = 0; j < n_kv; ++j) {
       if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
       const int st = j % NS;
@@ -182,25 +202,18 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         *abort_flag = 1;
         break;
       }
+      const int id = id_next;
+      if (j + 1 < n_kv) id_next = load_id(j + 1);
       if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kKVBytes);
       __syncwarp();
       if (lane < 8) {
-        const int blk = 8 * j + lane;
-        int id = fill_ok;  // keys past the sequence: finite filler data, masked to p = 0
-        if (blk < nblk_seq) {
-          id = bt[int64_t(r) * bt_stride + blk];
-          if (id < 0 || id >= num_blocks) {
-            flag_status(status, kStatusBadBlockId);
-            id = fill_ok;
-          }
-        }
         uint8_t* kdst = smem + Cfg::kOffKV + st * 2 * Cfg::kKVBytes + lane * 2048;
         uint8_t* vdst = kdst + Cfg::kKVBytes;
 #pragma unroll
-        for (int s = 0; s < Cfg::kSub; ++s) {
-          tma_load_4d(kdst + s * Cfg::kSubBytes, &tmap_k, &bars->kv_full[st], s * 64, g, 0, id,
+        for (int sb = 0; sb < Cfg::kSub; ++sb) {
+          tma_load_4d(kdst + sb * Cfg::kSubBytes, &tmap_k, &bars->kv_full[st], sb * 64, g, 0, id,
                       pol_kv);
-          tma_load_4d(vdst + s * Cfg::kSubBytes, &tmap_v, &bars->kv_full[st], s * 64, g, 0, id,
+          tma_load_4d(vdst + sb * Cfg::kSubBytes, &tmap_v, &bars->kv_full[st], sb * 64, g, 0, id,
                       pol_kv);
         }
       }
@@ -234,12 +247,39 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         issue_s(0);
         tc::commit(&bars->s_full);
       }
+      // S(j+1) needs tile j+1's K/V and the softmax warps' copy of S(j); PV(j) needs
+      // P(j).  Poll both and issue whichever is ready first, so PV(j) never waits
+      // behind the next tile's load (that load can only start once a stage frees).
       for (int j = 0; ok && j < n_kv; ++j) {
         if (aborted(abort_flag)) break;
         const int st = j % NS;
-        if (j + 1 < n_kv) {
-          const int st1 = (j + 1) % NS;
-          if (!mbar_wait(&bars->kv_full[st1], ((j + 1) / NS) & 1, status) ||
+        bool s_next = j + 1 >= n_kv;  // nothing to issue after the last tile
+        const int st1 = (j + 1) % NS;
+        const uint32_t kv_par = ((j + 1) / NS) & 1;
+        const uint64_t t0 = global_timer_ns();
+        bool pv_ready = false;
+        for (uint32_t spin = 0; !pv_ready; ++spin) {
+          if (!s_next && mbar_try_wait(&bars->kv_full[st1], kv_par) &&
+              mbar_try_wait(&bars->s_free, j & 1)) {
+            tc::fence_after_sync();
+            issue_s(st1);
+            tc::commit(&bars->s_full);
+            s_next = true;
+          }
+          pv_ready = mbar_try_wait(&bars->p_full, j & 1);
+          if (!pv_ready && (spin & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+            flag_status(status, kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        tc::fence_after_sync();
+        issue_pv(st, j > 0);
+        tc::commit(&bars->pv_done);
+        tc::commit(&bars->kv_empty[st]);
+        if (!s_next) {
+          if (!mbar_wait(&bars->kv_full[st1], kv_par, status) ||
               !mbar_wait(&bars->s_free, j & 1, status)) {
             ok = false;
             break;
@@ -248,14 +288,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
           issue_s(st1);
           tc::commit(&bars->s_full);
         }
-        if (!mbar_wait(&bars->p_full, j & 1, status)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-        issue_pv(st, j > 0);
-        tc::commit(&bars->pv_done);
-        tc::commit(&bars->kv_empty[st]);
       }
       if (!ok) *abort_flag = 1;
       // every MMA this thread issued is complete before TMEM is released
@@ -283,28 +315,66 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       }
       tc::fence_after_sync();
       float x[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tc::ld_32x32b_x32(tS + trow + c * 32, v);
+      {
+        uint32_t v0[32], v1[32], v2[32], v3[32];
+        tc::ld_32x32b_x32(tS + trow + 0, v0);
+        tc::ld_32x32b_x32(tS + trow + 32, v1);
+        tc::ld_32x32b_x32(tS + trow + 64, v2);
+        tc::ld_32x32b_x32(tS + trow + 96, v3);
         tc::wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(v0[i]);
+          x[32 + i] = __uint_as_float(v1[i]);
+          x[64 + i] = __uint_as_float(v2[i]);
+          x[96 + i] = __uint_as_float(v3[i]);
+        }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_free);
 
-      const int lim = qpos - j * Cfg::kBN;  // keys c <= lim are visible
-      float mx = -INFINITY;
+      // Raw scores; masked only where the causal diagonal or the sequence end cuts
+      // this tile (keys c <= lim are visible).
+      const int lim = qpos - j * Cfg::kBN;
+      if (lim < Cfg::kBN - 1) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        x[c] = (c <= lim) ? x[c] * scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = fast_exp2(m - m_new);
-      m = m_new;
+      // row max as a tree (8 independent chains), not one 128-long dependency chain
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = x[i];
+#pragma unroll
+      for (int c = 8; c < 128; c += 8) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mp[i] = fmaxf(mp[i], x[c + i]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      // Lazy max (one row per thread, no cross-lane work): scores are exponentiated
+      // against the reference max m (log2 units) unless this tile beats it by more
+      // than 2^8; only then do m, l and the row of O in TMEM get rescaled.
+      float alpha = 1.f;
+      if (mx * scale_log2 > m + kLazySlack) {
+        const float m_new = mx * scale_log2;
+        alpha = fast_exp2(m - m_new);
+        m = m_new;
+      }
+      const float neg_m = -m;
+      // P for this tile, packed to the element type, computed before waiting for the
+      // previous tile's PV MMA (which still reads the P buffer) so the exponentials
+      // overlap it.
+      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial sums
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = fast_exp2(fmaf(x[2 * c], scale_log2, neg_m));
+        const float p1 = fast_exp2(fmaf(x[2 * c + 1], scale_log2, neg_m));
+        sp[c & 7] += p0 + p1;
+        pk[c] = pack2<T>(p0, p1);
+      }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (j > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1, status))) {
           ok = false;
@@ -312,21 +382,13 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
         }
         tc::fence_after_sync();
       }
-      float sum = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < 16; ++c8) {
-        float p[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          p[i] = fast_exp2(x[c8 * 8 + i] - m_new);
-          sum += p[i];
-        }
         const int sub = c8 >> 3, cc = c8 & 7;
         const uint32_t addr = sP + sub * Cfg::kSubBytes + (row >> 3) * 1024 + (row & 7) * 128 +
                               ((cc ^ (row & 7)) << 4);
-        const uint4 v = pack8<T>(p);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
-                     "r"(v.z), "r"(v.w)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c8]),
+                     "r"(pk[4 * c8 + 1]), "r"(pk[4 * c8 + 2]), "r"(pk[4 * c8 + 3])
                      : "memory");
       }
       l = l * alpha + sum;
@@ -423,7 +485,8 @@ int launch_tc(void* out, const void* q, int64_t q_stride, const void* k_cache, c
   const int ntiles = (max_seqlen_q + tq - 1) / tq;
   dim3 grid(ntiles, Kh, R);
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
-      mq, mk, mv, static_cast<T*>(out), bt, bt_stride, cu, lk, H, group, num_blocks, max_blocks,
+      mq, mk, mv, static_cast<T*>(out),
+      bt, bt_stride, cu, lk, H, group, num_blocks, max_blocks,
       scale * kLog2e, device_status_ptr());
   return check_launch("as_varlen_prefill_attention (tcgen05)");
 }
