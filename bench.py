@@ -31,9 +31,18 @@ import torch
 
 REPO = Path(__file__).resolve().parent
 METRIC = "decode tok/s at 1/2/4/8 B200 + paged-attention achieved HBM GB/s"
-WORKLOAD = ("continuous-batching decode step, Llama-3.2-1B architecture (16 layers, hidden "
-            "2048, 32/8 heads, head_dim 64, FFN 8192, vocab 128256), bf16, random-init "
-            "N(0,0.02), 64 sequences per GPU, contexts U{128..4096}, 16-token blocks, greedy")
+WORKLOADS = {
+    "1b": ("continuous-batching decode step, Llama-3.2-1B architecture (16 layers, hidden "
+           "2048, 32/8 heads, head_dim 64, FFN 8192, vocab 128256), bf16, random-init "
+           "N(0,0.02), {batch} sequences per GPU, contexts U{{{lo}..{hi}}}, 16-token blocks, "
+           "greedy"),
+    "8b": ("8B-geometry decode step (32 layers, hidden 4096, 32/8 heads, head_dim 128, FFN "
+           "14336, vocab 128256), bf16, random-init N(0,0.02), {batch} sequences per GPU "
+           "(request-partitioned replicas; 8 GPUs x 32 = the 256-sequence configuration), "
+           "contexts U{{{lo}..{hi}}}, 16-token blocks, greedy"),
+}
+MODEL_DEFAULTS = {"1b": dict(batch=64, ctx_min=128, ctx_max=4096, layers=16, cpu_sample_seqs=8),
+                  "8b": dict(batch=32, ctx_min=1024, ctx_max=32768, layers=32, cpu_sample_seqs=2)}
 
 
 def parse():
@@ -42,17 +51,22 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--ctx-min", type=int, default=128)
-    ap.add_argument("--ctx-max", type=int, default=4096)
+    ap.add_argument("--model", default="1b", choices=["1b", "8b"])
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--ctx-min", type=int, default=None)
+    ap.add_argument("--ctx-max", type=int, default=None)
     ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--cpu-sample-seqs", type=int, default=8)
+    ap.add_argument("--cpu-sample-seqs", type=int, default=None)
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--blocks-per-split", type=int, default=0)
-    ap.add_argument("--layers", type=int, default=16, help=argparse.SUPPRESS)
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
+    args = ap.parse_args()
+    for k, v in MODEL_DEFAULTS[args.model].items():
+        if getattr(args, k) is None:
+            setattr(args, k, v)
+    return args
 
 
 def dist_env():
@@ -60,11 +74,19 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
-def model_config(layers: int = 16):
+def model_config(args):
     from agentserve_b200.config import ModelConfig
-    return ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=layers,
+    if args.model == "8b":
+        return ModelConfig(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=args.layers,
+                           vocab_size=128256, max_seq_len=33024 + 1024, rope_theta=500000.0,
+                           intermediate_size=14336)
+    return ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=args.layers,
                        vocab_size=128256, max_seq_len=8192, rope_theta=500000.0,
                        intermediate_size=8192)
+
+
+def workload(args) -> str:
+    return WORKLOADS[args.model].format(batch=args.batch, lo=args.ctx_min, hi=args.ctx_max)
 
 
 def context_lengths(batch, lo, hi, seed):
@@ -123,7 +145,7 @@ def cpu_baseline(args, steps: int, warmup: int, seqs: int):
     from oracle.paged import OracleBlockAllocator
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = model_config(args.layers)
+    cfg = model_config(args)
     m = OracleLlama(cfg)
     g = torch.Generator().manual_seed(1234)
     with torch.no_grad():
@@ -159,9 +181,10 @@ def cpu_baseline(args, steps: int, warmup: int, seqs: int):
     except OSError:
         pass
     return {"value": len(lens) * steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": (f"oracle port of forward_decode_paged, fp32, {len(lens)} of the 64 "
-                       f"sequences (contexts {min(lens)}-{max(lens)}), {steps} timed steps after "
-                       f"{warmup} warm-up, full 16-layer geometry, CPU {cpu_model}"),
+            "sample": (f"oracle port of forward_decode_paged, fp32, {len(lens)} of the "
+                       f"{args.batch} sequences (contexts {min(lens)}-{max(lens)}), {steps} timed "
+                       f"steps after {warmup} warm-up, full {cfg.n_layers}-layer geometry, "
+                       f"CPU {cpu_model}"),
             "seconds": dt}
 
 
@@ -265,7 +288,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": WORKLOAD,
+            "data": "synthetic", "config": {"workload": workload(args),
                                             "sample": cb["sample"]},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -284,7 +307,7 @@ def run_b200(args):
                                 device_id=dev)
     from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, greedy, ops
 
-    cfg = model_config(args.layers)
+    cfg = model_config(args)
     B = args.batch
     model = B200LlamaModel(cfg, dtype=torch.bfloat16, device=dev)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -395,7 +418,10 @@ def run_b200(args):
     if world > 1:
         torch.distributed.barrier()
     if rank == 0:
-        traffic = load_traffic()
+        kv_gb = cfg.n_layers * decode_attention_bytes(lk, cfg.n_heads, cfg.n_kv_heads,
+                                                      cfg.head_dim, 2) / 1e9
+        w_gb = sum(p.numel() for p in model.parameters()) * 2 / 1e9
+        traffic = load_traffic() if args.model == "1b" else None
         traffic_launch = None
         if traffic:
             traffic_launch = (traffic["dram_bytes_per_launch"] * abytes
@@ -405,13 +431,15 @@ def run_b200(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * world,
+            "config": {"workload": workload(args), "global_batch": B * world,
                        "seq_len": f"{args.ctx_min}-{args.ctx_max} context + decode",
                        "parallelism": f"{world} request-partitioned replicas, no collective",
                        "cuda_graph": True, "blocks_per_split": bps,
-                       "l2": "inputs larger than L2 every step (~4.4 GB KV + ~3 GB weights)",
+                       "l2": (f"inputs larger than L2 every step (~{kv_gb:.1f} GB KV + "
+                              f"~{w_gb:.1f} GB weights)"),
                        "kv": "context KV synthesised N(0,1) into the pool"},
-            "roofline": {"kernel": "paged_decode_attention (bf16, D=64, GQA 4)", "bound": "hbm",
+            "roofline": {"kernel": f"paged_decode_attention (bf16, D={cfg.head_dim}, GQA "
+                                   f"{cfg.n_heads // cfg.n_kv_heads})", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": abytes, "launch_ms": attn_ms,
