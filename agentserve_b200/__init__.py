@@ -9,6 +9,6 @@ mirrors the reference's model/allocator interface so AgentServe's Engine can use
 from . import _native, ops  # noqa: F401
 from .cache import DeviceBlockAllocator  # noqa: F401
 from .config import ModelConfig, TinyConfig, Llama32_1B, Llama32_3B, Llama32_8B, llama_8b_long  # noqa: F401
-from .model import B200LlamaModel, DecodeGraph, greedy  # noqa: F401
+from .model import B200LlamaModel, DecodeGraph, greedy, shard_state_dict  # noqa: F401
 
 __version__ = "0.1.0"

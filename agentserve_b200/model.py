@@ -59,9 +59,9 @@ class RMSNorm(nn.Module):
 
 
 class _Attn(nn.Module):
-    def __init__(self, c):
+    def __init__(self, c, tp_size: int = 1):
         super().__init__()
-        H, Kh, D = c.n_heads, c.n_kv_heads, c.head_dim
+        H, Kh, D = c.n_heads // tp_size, c.n_kv_heads // tp_size, c.head_dim
         self.q_proj = nn.Linear(c.hidden_dim, H * D, bias=False)
         self.k_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
         self.v_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
@@ -77,23 +77,66 @@ class _MLP(nn.Module):
 
 
 class _Layer(nn.Module):
-    def __init__(self, c):
+    def __init__(self, c, tp_size: int = 1):
         super().__init__()
         self.attn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
-        self.attn = _Attn(c)
+        self.attn = _Attn(c, tp_size)
         self.ffn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
         self.ffn = _MLP(c)
 
 
+def shard_state_dict(full: dict, config, tp_size: int, tp_rank: int,
+                     reference_compat: bool = True) -> dict:
+    """KV-head tensor parallelism: the state dict of rank tp_rank out of tp_size.
+
+    Rank r keeps query heads [r*H/N, (r+1)*H/N) and KV heads [r*Kh/N, (r+1)*Kh/N) (a
+    GQA group never straddles ranks), i.e. row slices of q/k/v_proj, and the o_proj
+    columns its heads feed.  Those columns are contiguous for the head-major flatten
+    (h*D + d), and strided for the reference decode's dim-major flatten (d*H + h):
+    the rank's local attention output is d*H_l + h_l, so its o_proj shard is
+    W[:, d*H + r*H_l + h_l] in that order.  Everything else is replicated."""
+    H, Kh, D = config.n_heads, config.n_kv_heads, config.head_dim
+    if H % tp_size or Kh % tp_size:
+        raise ValueError(f"{tp_size} ranks cannot split {H} query / {Kh} KV heads")
+    Hl, Khl = H // tp_size, Kh // tp_size
+    out = {}
+    if reference_compat:
+        d = torch.arange(D).view(D, 1)
+        h = torch.arange(Hl).view(1, Hl) + tp_rank * Hl
+        ocols = (d * H + h).reshape(-1)
+    else:
+        ocols = torch.arange(tp_rank * Hl * D, (tp_rank + 1) * Hl * D)
+    for name, w in full.items():
+        if name.endswith("attn.q_proj.weight"):
+            out[name] = w[tp_rank * Hl * D:(tp_rank + 1) * Hl * D]
+        elif name.endswith("attn.k_proj.weight") or name.endswith("attn.v_proj.weight"):
+            out[name] = w[tp_rank * Khl * D:(tp_rank + 1) * Khl * D]
+        elif name.endswith("attn.o_proj.weight"):
+            out[name] = w[:, ocols.to(w.device)]
+        else:
+            out[name] = w
+    return {k: v.contiguous() for k, v in out.items()}
+
+
 class B200LlamaModel(nn.Module):
+    """tp_size > 1: KV-head tensor parallelism over tp_group (one process per GPU):
+    this rank holds H/N query and Kh/N KV heads of every sequence (its allocator holds
+    Kh/N heads too), o_proj is row-parallel and its output is summed over the group
+    with one all-reduce per layer; the MLP, embedding and lm_head are replicated.
+    Build the weights with shard_state_dict()."""
+
     def __init__(self, config, dtype: torch.dtype = torch.bfloat16,
                  device: str | torch.device = "cuda", fused_projections: bool = True,
-                 reference_compat: bool = True):
+                 reference_compat: bool = True, tp_size: int = 1, tp_rank: int = 0,
+                 tp_group=None):
         super().__init__()
         c = self.config = config
-        self.H, self.Kh, self.D = c.n_heads, c.n_kv_heads, c.head_dim
+        if c.n_heads % tp_size or c.n_kv_heads % tp_size:
+            raise ValueError(f"{tp_size} ranks cannot split {c.n_heads}/{c.n_kv_heads} heads")
+        self.tp_size, self.tp_rank, self.tp_group = tp_size, tp_rank, tp_group
+        self.H, self.Kh, self.D = c.n_heads // tp_size, c.n_kv_heads // tp_size, c.head_dim
         self.embed = nn.Embedding(c.vocab_size, c.hidden_dim)
-        self.layers = nn.ModuleList([_Layer(c) for _ in range(c.n_layers)])
+        self.layers = nn.ModuleList([_Layer(c, tp_size) for _ in range(c.n_layers)])
         self.norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
         self.lm_head = nn.Linear(c.hidden_dim, c.vocab_size, bias=False)
         self.to(device=device, dtype=dtype)
@@ -167,6 +210,8 @@ class B200LlamaModel(nn.Module):
         h = ops.rmsnorm(x, self.layers[0].attn_norm.weight, self.layers[0].attn_norm.eps)
         for li, layer in enumerate(self.layers):
             a = layer.attn.o_proj(attention(li, layer, h))
+            if self.tp_size > 1:  # row-parallel o_proj: sum the ranks' partial outputs
+                torch.distributed.all_reduce(a, group=self.tp_group)
             h = ops.add_rmsnorm(x, a, layer.ffn_norm.weight, layer.ffn_norm.eps)
             nxt = self.layers[li + 1].attn_norm if li + 1 < L else self.norm
             h = ops.add_rmsnorm(x, self._mlp(layer, h), nxt.weight, nxt.eps)

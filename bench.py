@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--blocks-per-split", type=int, default=0)
+    ap.add_argument("--tp", action="store_true",
+                    help="KV-head tensor parallelism over all ranks instead of replicas")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     for k, v in MODEL_DEFAULTS[args.model].items():
@@ -308,20 +310,28 @@ def run_b200(args):
     from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, greedy, ops
 
     cfg = model_config(args)
-    B = args.batch
-    model = B200LlamaModel(cfg, dtype=torch.bfloat16, device=dev)
-    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    tp = world if args.tp else 1
+    # replicas: every rank decodes its own `batch` sequences; KV-head TP: all ranks
+    # decode the same batch * world sequences, each holding 1/world of the KV heads
+    B = args.batch * tp
+    model = B200LlamaModel(cfg, dtype=torch.bfloat16, device=dev, tp_size=tp,
+                           tp_rank=rank if tp > 1 else 0)
+    sharded = ("q_proj", "k_proj", "v_proj", "o_proj")
     with torch.no_grad():
-        for n, p in model.named_parameters():
+        for i, (n, p) in enumerate(model.named_parameters()):
             if p.dim() == 2:
-                p.normal_(0.0, 0.02, generator=gen)
+                own = tp > 1 and any(k in n for k in sharded)
+                g = torch.Generator(device=dev).manual_seed(
+                    1000 + i + (rank if (tp == 1 or own) else 0) * 100003)
+                p.normal_(0.0, 0.02, generator=g)
+    gen = torch.Generator(device=dev).manual_seed(77 + (rank if tp == 1 else 0))
     model.eval()
     model.fuse_projections_()
 
-    lens = context_lengths(B, args.ctx_min, args.ctx_max, seed=rank)
+    lens = context_lengths(B, args.ctx_min, args.ctx_max, seed=rank if tp == 1 else 0)
     horizon = args.warmup + args.steps + args.e2e_steps + 4
     nblk = [(L + horizon + 15) // 16 for L in lens]
-    alloc = DeviceBlockAllocator(sum(nblk), 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+    alloc = DeviceBlockAllocator(sum(nblk), 16, cfg.n_layers, model.Kh, cfg.head_dim,
                                  dtype=torch.bfloat16, device=dev, max_seqs=B,
                                  max_blocks_per_seq=max(nblk))
     alloc.kv_pool.normal_(0.0, 1.0, generator=gen)  # synthesised context KV
@@ -332,7 +342,8 @@ def run_b200(args):
     max_blocks = max(nblk)
     bps = args.blocks_per_split  # 0: balanced persistent partition
     model.decode_blocks_per_split = bps
-    tokens0 = torch.randint(3, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(7 + rank))
+    tokens0 = torch.randint(3, cfg.vocab_size, (B,),
+                            generator=torch.Generator().manual_seed(7 + (rank if tp == 1 else 0)))
 
     def barrier():
         if world > 1:
@@ -364,7 +375,7 @@ def run_b200(args):
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
-    value = world * B * args.steps / (ms / 1e3)
+    value = (world // tp) * B * args.steps / (ms / 1e3)
 
     # ---------------- end to end through forward_decode_paged with host lists
     cur = [L + args.warmup + args.steps for L in lens]
@@ -385,15 +396,15 @@ def run_b200(args):
         cur = [x + 1 for x in cur]
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e_value = world * B * (e2e_steps - 2) / e2e_s
+    e2e_value = (world // tp) * B * (e2e_steps - 2) / e2e_s
 
     # ---------------- paged decode attention kernel alone (roofline)
     seq_lens = torch.tensor(cur, dtype=torch.int32, device=dev)
     rows_t = torch.tensor(rows, dtype=torch.int32, device=dev)
     pk = ops.pack_decode(alloc.block_tables, seq_lens, rows_t, max_blocks)
-    q = torch.randn(B, cfg.n_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
-    ws = ops.new_decode_workspace(B, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, max_blocks, bps, dev)
-    out = torch.empty(B, cfg.n_heads * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(B, model.H, cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    ws = ops.new_decode_workspace(B, model.H, model.Kh, cfg.head_dim, max_blocks, bps, dev)
+    out = torch.empty(B, model.H * cfg.head_dim, device=dev, dtype=torch.bfloat16)
     reps = 3 * cfg.n_layers
     for li in range(cfg.n_layers):  # warm
         ops.paged_decode_attention(q, alloc.k_plane(li), alloc.v_plane(li), pk.block_tables,
@@ -409,16 +420,16 @@ def run_b200(args):
     torch.cuda.synchronize()
     attn_ms = a0.elapsed_time(a1) / reps
     lk = [x + 1 for x in cur]
-    abytes = decode_attention_bytes(lk, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, 2)
+    abytes = decode_attention_bytes(lk, model.H, model.Kh, cfg.head_dim, 2)
     achieved = abytes / (attn_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
-    pf = measure_prefill(dev) if not args.no_prefill else None
+    pf = measure_prefill(dev) if not args.no_prefill and tp == 1 else None
     bits = ops.device_status(clear=True)
 
     if world > 1:
         torch.distributed.barrier()
     if rank == 0:
-        kv_gb = cfg.n_layers * decode_attention_bytes(lk, cfg.n_heads, cfg.n_kv_heads,
+        kv_gb = cfg.n_layers * decode_attention_bytes(lk, model.H, model.Kh,
                                                       cfg.head_dim, 2) / 1e9
         w_gb = sum(p.numel() for p in model.parameters()) * 2 / 1e9
         traffic = load_traffic() if args.model == "1b" else None
@@ -431,15 +442,19 @@ def run_b200(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": workload(args), "global_batch": B * world,
+            "config": {"workload": workload(args), "global_batch": B * (world // tp),
                        "seq_len": f"{args.ctx_min}-{args.ctx_max} context + decode",
-                       "parallelism": f"{world} request-partitioned replicas, no collective",
+                       "parallelism": (f"KV-head tensor parallel over {world} GPUs, one NCCL "
+                                       f"all-reduce per layer after o_proj, MLP replicated"
+                                       if tp > 1 else
+                                       f"{world} request-partitioned replicas, no collective"),
                        "cuda_graph": True, "blocks_per_split": bps,
                        "l2": (f"inputs larger than L2 every step (~{kv_gb:.1f} GB KV + "
                               f"~{w_gb:.1f} GB weights)"),
                        "kv": "context KV synthesised N(0,1) into the pool"},
             "roofline": {"kernel": f"paged_decode_attention (bf16, D={cfg.head_dim}, GQA "
-                                   f"{cfg.n_heads // cfg.n_kv_heads})", "bound": "hbm",
+                                   f"{model.H // model.Kh}, {model.Kh} KV heads per GPU)",
+                         "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": abytes, "launch_ms": attn_ms,
