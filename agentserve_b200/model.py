@@ -23,6 +23,7 @@ keeps the new token's K/V.
 from __future__ import annotations
 
 import math
+from collections import OrderedDict
 from typing import List, Optional, Sequence
 
 import torch
@@ -149,9 +150,15 @@ class B200LlamaModel(nn.Module):
         self.decode_layout = N.AS_LAYOUT_DIM_MAJOR if reference_compat else N.AS_LAYOUT_HEAD_MAJOR
         self._fused = False
         self._workspaces = {}
-        # decode attention work split: 0 = balanced persistent partition of all
-        # (sequence, KV head, block) units (default); > 0 = fixed split-K chunk in blocks
+        # decode attention split-K chunk in blocks: 0 = chosen by the library from the
+        # batch's block count and the SM count (default); > 0 = fixed chunk
         self.decode_blocks_per_split: int = 0
+        # forward_decode_paged replays a CUDA graph per (allocator, batch size, block
+        # bucket) instead of launching ~5 kernels per layer from Python every step
+        self.decode_graphs: bool = True
+        self.max_decode_graphs: int = 16
+        self._graphs: "OrderedDict[tuple, _PagedStepGraph]" = OrderedDict()
+        self._graph_pool = None
 
     @property
     def device(self) -> torch.device:
@@ -271,6 +278,54 @@ class B200LlamaModel(nn.Module):
         h = self._run_layers(x, attention)
         return self._logits(h), new_cache
 
+    # ------------------------------------------------------------------ prefill (paged)
+    @torch.inference_mode()
+    def forward_prefill_paged(self, token_ids: Sequence[Sequence[int]],
+                              num_cached: Sequence[int], allocator, request_ids: Sequence[str]):
+        """Batched varlen prefill straight into the allocator's pool: request r's first
+        num_cached[r] tokens are already in its blocks (a prefix-cache hit seeded with
+        DeviceBlockAllocator.seed_blocks, engine.py:274-281) and the rest are computed
+        here in one forward for all requests (the reference runs one request per forward,
+        engine.py:228-229, then write_kv_prefill per layer, engine.py:311-315).  As in
+        engine.py:299-302, a fully cached prompt re-feeds its last token at position
+        len(prompt).  Returns the logits of each request's last token [R, V]."""
+        if not isinstance(allocator, DeviceBlockAllocator):
+            raise TypeError("forward_prefill_paged needs an agentserve_b200.DeviceBlockAllocator")
+        self.fuse_projections_()
+        R = len(token_ids)
+        if R == 0:
+            return torch.zeros(0, self.config.vocab_size)
+        dev = self.device
+        new_tok, nc, nn_ = [], [], []
+        for toks, c in zip(token_ids, num_cached):
+            c = int(c)
+            rest = list(toks[c:])
+            if not rest:  # engine.py:300-302: feed the last token again
+                rest = list(toks[-1:])
+            new_tok.extend(rest)
+            nc.append(c)
+            nn_.append(len(rest))
+        total = len(new_tok)
+        rows = allocator.rows_for(request_ids)
+        meta = torch.tensor([nc, nn_, rows], dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        tokens = torch.tensor(new_tok, dtype=torch.long).pin_memory().to(dev, non_blocking=True)
+        max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
+        pk = ops.pack_prefill(allocator.block_tables, meta[0].contiguous(), meta[1].contiguous(),
+                              total, meta[2].contiguous(), max_blocks)
+        max_new = max(nn_)
+
+        def attention(li, layer, h):
+            q, k, v = self._qkv(layer, h)
+            kp, vp = allocator.k_plane(li), allocator.v_plane(li)
+            ops.rope_reshape_and_cache(q, k, v, pk.positions, pk.slot_mapping, self.rope_table,
+                                       kp, vp)
+            return ops.varlen_prefill_attention(q, kp, vp, pk.block_tables, pk.cu_seqlens_q,
+                                                pk.seq_lens_k, max_new, self.scale)
+
+        h = self._run_layers(self.embed(tokens), attention)
+        last = pk.cu_seqlens_q[1:].long() - 1
+        return self._logits(h.index_select(0, last))
+
     # ------------------------------------------------------------------ decode (lists)
     @torch.inference_mode()
     def forward_decode_batch(self, last_token_ids: List[int], kv_caches: list,
@@ -332,14 +387,17 @@ class B200LlamaModel(nn.Module):
     # ------------------------------------------------------------------ decode (paged)
     def _decode_core(self, tokens: torch.Tensor, seq_lens: torch.Tensor, row_ids: torch.Tensor,
                      allocator: DeviceBlockAllocator, max_blocks: int, bps: int,
-                     positions: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     positions: Optional[torch.Tensor] = None,
+                     ws: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step entirely on the device (no host sync): pack -> per layer
         (norm, fused QKV GEMM, fused RoPE+cache write, paged attention, o_proj,
-        MLP) -> norm -> lm_head.  Returns logits [B, V]."""
+        MLP) -> norm -> lm_head.  Returns logits [B, V].  A CUDA graph passes its own
+        split-K workspace `ws` (the shared one may be reallocated by later calls)."""
         B = tokens.shape[0]
         pk = ops.pack_decode(allocator.block_tables, seq_lens, row_ids, max_blocks)
         pos = pk.positions if positions is None else positions
-        ws = self._workspace(B, max_blocks, bps)
+        if ws is None:
+            ws = self._workspace(B, max_blocks, bps)
 
         def attention(li, layer, h):
             q, k, v = self._qkv(layer, h)
@@ -365,6 +423,12 @@ class B200LlamaModel(nn.Module):
             return torch.zeros(0, self.config.vocab_size), None
         dev = self.device
         rows = allocator.rows_for(request_ids)
+        max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
+        bps = self.decode_blocks_per_split
+        if (self.decode_graphs and dev.type == "cuda" and
+                list(position_offsets) == list(seq_lens)):
+            return self._graphed_decode(allocator, last_token_ids, seq_lens, rows, max_blocks,
+                                        bps), None
         host = torch.tensor([list(last_token_ids), list(seq_lens), rows, list(position_offsets)],
                             dtype=torch.int64).pin_memory()
         d = host.to(dev, non_blocking=True)
@@ -372,10 +436,85 @@ class B200LlamaModel(nn.Module):
         sl = d[1].to(torch.int32)
         rid = d[2].to(torch.int32)
         pos = None if list(position_offsets) == list(seq_lens) else d[3].contiguous()
-        max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
-        bps = self.decode_blocks_per_split
         logits = self._decode_core(tokens, sl, rid, allocator, max_blocks, bps, positions=pos)
         return logits, None
+
+
+    def _graphed_decode(self, allocator, tokens, seq_lens, rows, max_blocks: int,
+                        bps: int) -> torch.Tensor:
+        """forward_decode_paged through a cached CUDA graph.  Graphs are keyed by the
+        allocator, the batch size and max_blocks rounded up to a power of two (capped by
+        the allocator's table width); the split-K decomposition follows that bucket.
+        Least recently used graphs beyond max_decode_graphs are released."""
+        B = len(tokens)
+        cap = allocator.block_tables.shape[1]
+        mb = min(cap, 1 << max(0, (max_blocks - 1).bit_length()))
+        key = (id(allocator), B, mb, bps)
+        g = self._graphs.get(key)
+        if g is None or g.allocator is not allocator:
+            if self._graph_pool is None:
+                self._graph_pool = torch.cuda.graph_pool_handle()
+            g = _PagedStepGraph(self, allocator, B, mb, bps, self._graph_pool)
+            self._graphs[key] = g
+            while len(self._graphs) > self.max_decode_graphs:
+                self._graphs.popitem(last=False)
+        self._graphs.move_to_end(key)
+        return g.run(tokens, seq_lens, rows)
+
+    def release_decode_graphs(self) -> None:
+        """Drop every cached decode graph (e.g. before destroying a process group whose
+        all-reduce the graphs captured)."""
+        self._graphs.clear()
+        self._graph_pool = None
+
+
+class _PagedStepGraph:
+    """One captured forward_decode_paged step (logits only) for a fixed batch size and
+    block bucket.  Inputs travel in one pinned int32 [3, B] buffer (tokens, seq_lens,
+    table rows) with one host-to-device copy per call."""
+
+    def __init__(self, model: "B200LlamaModel", allocator: DeviceBlockAllocator, B: int,
+                 max_blocks: int, bps: int, pool):
+        self.allocator = allocator
+        dev = model.device
+        self.host = torch.zeros(3, B, dtype=torch.int32).pin_memory()
+        self.inputs = torch.zeros(3, B, dtype=torch.int32, device=dev)
+        self.copied = torch.cuda.Event()
+        self.ws = ops.new_decode_workspace(B, model.H, model.Kh, model.D, max_blocks, bps, dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+        def body():
+            return model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
+                                      allocator, max_blocks, bps, ws=self.ws)
+
+        self._body = body
+        self._pool = pool
+        self.logits: Optional[torch.Tensor] = None
+
+    def _stage(self, tokens, seq_lens, rows) -> None:
+        self.copied.synchronize()  # the previous call's copy has left the pinned buffer
+        h = self.host.numpy()
+        h[0], h[1], h[2] = tokens, seq_lens, rows
+        self.inputs.copy_(self.host, non_blocking=True)
+        self.copied.record()
+
+    @torch.inference_mode()
+    def run(self, tokens, seq_lens, rows) -> torch.Tensor:
+        self._stage(tokens, seq_lens, rows)
+        if self.graph is None:
+            # warm-up on a side stream (kernel attributes, cuBLAS workspaces), then
+            # capture; the warm-up writes the same pool slots the replay rewrites
+            s = torch.cuda.Stream(device=self.inputs.device)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                self._body()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, pool=self._pool):
+                self.logits = self._body()
+        self.graph.replay()
+        return self.logits.clone()
 
 
 def greedy(logits: torch.Tensor) -> torch.Tensor:

@@ -383,7 +383,7 @@ def run_b200(args):
     del graph
     torch.cuda.synchronize()
     e2e_steps = max(3, args.e2e_steps)
-    for _ in range(2):  # warm the eager path (its own CUDA graph buckets, cuBLAS)
+    for _ in range(2):  # capture forward_decode_paged's graph for this batch
         lg, _ = model.forward_decode_paged(last, cur, cur, alloc, rids)
         last = greedy(lg).cpu().tolist()
         cur = [x + 1 for x in cur]
@@ -481,6 +481,8 @@ def run_b200(args):
                               seqs=args.cpu_sample_seqs)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
+    model.release_decode_graphs()  # they captured this group's all-reduce
+    torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

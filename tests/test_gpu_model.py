@@ -15,6 +15,7 @@ from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, g
 from agentserve_b200.config import ModelConfig
 from oracle.model import OracleLlama
 from oracle.paged import OracleBlockAllocator
+from oracle.rope import precompute_rope_freqs
 from oracle.weights import init_weights_
 from tests.golden import scenarios as S
 
@@ -165,3 +166,130 @@ def test_decode_graph_matches_eager_bf16():
     for _ in range(steps):
         graphed.append(dg.replay().tolist())
     assert graphed == eager
+
+
+PAGED_CFG = dict(hidden_dim=256, n_heads=4, n_kv_heads=2, n_layers=2, vocab_size=512,
+                 max_seq_len=1024, rope_theta=10000.0, intermediate_size=512)
+
+
+def _oracle_prefill(o, p, c):
+    """engine.py:297-307 for one request whose first c tokens hit the prefix cache."""
+    pre = o.forward(p[:c])[1] if c else None
+    rest = p[c:] or p[-1:]
+    lg, kv = o.forward(rest, kv_cache=pre, position_offset=c)
+    return lg[-1], kv
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_batched_paged_prefill_with_seeded_prefixes(dtype):
+    """forward_prefill_paged over requests with no, partial (block-aligned and ragged)
+    and full prefix hits, the prefixes seeded device-side with gather_blocks ->
+    seed_blocks: last-token logits and the pool contents match the oracle's per-request
+    prefill (engine.py:297-315), and decoding continues from the pool."""
+    cfg = ModelConfig(**PAGED_CFG)
+    m = b200_model(cfg, dtype, fused=True)
+    o = OracleLlama(cfg).to(DEV)
+    init_weights_(o, seed=0)
+    o = o.to(dtype).eval()
+    o.rope_table = o.rope_table.float() if dtype == torch.float32 else \
+        precompute_rope_freqs(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta).to(DEV)
+    g = torch.Generator().manual_seed(11)
+    lens = [70, 33, 150, 16, 48, 400]
+    cached = [0, 32, 101, 16, 0, 257]  # block-aligned, ragged, full (16 of 16), none
+    prompts = [torch.randint(3, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    a = DeviceBlockAllocator(256, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                             dtype=dtype, device=DEV)
+    rids = [f"p{i}" for i in range(len(prompts))]
+    for i, (p, c) in enumerate(zip(prompts, cached)):
+        if c:  # a donor request fills the prefix, then its blocks seed the target's
+            a.allocate(f"d{i}", a.blocks_needed(c))
+            m.forward_prefill_paged([p[:c]], [0], a, [f"d{i}"])
+            payload = a.gather_blocks(f"d{i}", a.blocks_needed(c))
+            a.free(f"d{i}")
+        a.allocate(rids[i], a.blocks_needed(len(p) + 8))
+        if c:
+            a.seed_blocks(rids[i], payload)
+    logits = m.forward_prefill_paged(prompts, cached, a, rids)
+    assert logits.shape == (len(prompts), cfg.vocab_size)
+    atol = 2e-4 if dtype == torch.float32 else 6e-2
+    kv_atol = 1e-4 if dtype == torch.float32 else 3e-2
+    for i, (p, c) in enumerate(zip(prompts, cached)):
+        lo, kvo = _oracle_prefill(o, p, c)
+        torch.testing.assert_close(logits[i].float(), lo.float(), rtol=0, atol=atol)
+        n = len(p) + (1 if c == len(p) else 0)
+        for li in range(cfg.n_layers):
+            k, v = a.gather_kv(rids[i], n, li)
+            torch.testing.assert_close(k.float(), kvo[li][0].float(), rtol=0, atol=kv_atol)
+            torch.testing.assert_close(v.float(), kvo[li][1].float(), rtol=0, atol=kv_atol)
+    if dtype == torch.float32:  # greedy continuation from the pool matches the oracle
+        oa = OracleBlockAllocator(256, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                                  allocate_tensor=True, device=DEV)
+        last, pos = [], []
+        for i, (p, c) in enumerate(zip(prompts, cached)):
+            lo, kvo = _oracle_prefill(o, p, c)
+            oa.allocate(rids[i], oa.blocks_needed(len(p) + 8))
+            for li in range(cfg.n_layers):
+                oa.write_kv_prefill(rids[i], li, *kvo[li])
+            last.append(int(lo.argmax()))
+            pos.append(kvo[0][0].shape[0])
+        assert greedy(logits).tolist() == last
+        lm_last = list(last)
+        for _ in range(4):
+            lm, _ = m.forward_decode_paged(lm_last, pos, pos, a, rids)
+            lo, _ = o.forward_decode_paged(last, pos, pos, oa, rids)
+            torch.testing.assert_close(lm, lo, rtol=0, atol=atol)
+            lm_last, last = greedy(lm).tolist(), greedy(lo).tolist()
+            assert lm_last == last
+            pos = [x + 1 for x in pos]
+
+
+@pytest.mark.parametrize("bps", [8, 0])
+def test_forward_decode_paged_graphs_match_eager(bps):
+    """forward_decode_paged's cached CUDA graphs (keyed by batch size and block bucket)
+    give the eager path's logits while batch size, lengths and buckets change between
+    calls; with a fixed split-K chunk the two are bit-identical."""
+    cfg = ModelConfig(hidden_dim=1024, n_heads=16, n_kv_heads=4, n_layers=2, vocab_size=1000,
+                      max_seq_len=4096, rope_theta=500000.0, intermediate_size=1024)
+    m = b200_model(cfg, torch.bfloat16, fused=True)
+    m.decode_blocks_per_split = bps
+    g = torch.Generator().manual_seed(9)
+    lens = torch.randint(5, 900, (10,), generator=g).tolist()
+    toks = torch.randint(3, cfg.vocab_size, (10,), generator=g).tolist()
+    rids = [f"q{i}" for i in range(10)]
+    pool0 = None
+    # batch composition per call: shrink, grow, and one long sequence that moves the
+    # block bucket from 64 to 128
+    plan = [range(10), range(10), range(7), range(7), range(10), range(3)]
+
+    def run(graphs):
+        nonlocal pool0
+        a = DeviceBlockAllocator(1024, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                                 dtype=torch.bfloat16, device=DEV, max_blocks_per_seq=160)
+        if pool0 is None:
+            pool0 = torch.randn(a.kv_pool.shape, generator=g).to(torch.bfloat16)
+        a.kv_pool.copy_(pool0)
+        for r, L in zip(rids, lens):
+            a.allocate(r, a.blocks_needed(L + 40))
+        m.decode_graphs = graphs
+        cur = list(lens)
+        outs = []
+        for step, sel in enumerate(plan):
+            sel = list(sel)
+            if step == 4:
+                a.allocate("q0", 80)  # q0 now spans more than 64 blocks
+            lg, _ = m.forward_decode_paged([toks[i] for i in sel], [cur[i] for i in sel],
+                                           [cur[i] for i in sel], a, [rids[i] for i in sel])
+            outs.append(lg.float().cpu())
+            for i in sel:
+                cur[i] += 1
+        return outs
+
+    eager = run(False)
+    graphed = run(True)
+    assert len(m._graphs) >= 4
+    for e, gr in zip(eager, graphed):
+        if bps:
+            assert torch.equal(e, gr)
+        else:
+            torch.testing.assert_close(gr, e, rtol=0, atol=2e-2)
+    m.release_decode_graphs()
