@@ -92,11 +92,13 @@ template <typename T, int D>
 __global__ void __launch_bounds__(192, PfCfg<D>::kMinBlocks)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                   const __grid_constant__ CUtensorMap tmap_k,
-                  const __grid_constant__ CUtensorMap tmap_v, T* __restrict__ out,
+                  const __grid_constant__ CUtensorMap tmap_v,
+                  const __grid_constant__ CUtensorMap tmap_k8,
+                  const __grid_constant__ CUtensorMap tmap_v8, T* __restrict__ out,
                   const int32_t* __restrict__ bt, int64_t bt_stride,
                   const int32_t* __restrict__ cu_seqlens_q, const int32_t* __restrict__ seq_lens_k,
                   int H, int group, int num_blocks, int max_blocks, float scale_log2,
-                  int* status) {
+                  int run8_ok, int* status) {
   using Cfg = PfCfg<D>;
   constexpr int NS = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -172,6 +174,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
+      tma_prefetch_desc(&tmap_k8);
+      tma_prefetch_desc(&tmap_v8);
       mbar_arrive_expect_tx(&bars->q_full, Cfg::kQBytes);
       const uint64_t pol_q = l2_policy_evict_first();
       for (int s = 0; s < Cfg::kSub; ++s)
@@ -204,9 +208,24 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
       }
       const int id = id_next;
       if (j + 1 < n_kv) id_next = load_id(j + 1);
+      // A tile whose 8 blocks are consecutive pool ids (a request's blocks handed out
+      // together by the FIFO free list) moves as one 16-block box per operand.
+      const int id0 = __shfl_sync(0xffffffffu, id, 0);
+      const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & 7));
       if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kKVBytes);
       __syncwarp();
-      if (lane < 8) {
+      if (run8) {
+        if (lane == 0) {
+          uint8_t* kdst = smem + Cfg::kOffKV + st * 2 * Cfg::kKVBytes;
+#pragma unroll
+          for (int sb = 0; sb < Cfg::kSub; ++sb) {
+            tma_load_4d(kdst + sb * Cfg::kSubBytes, &tmap_k8, &bars->kv_full[st], sb * 64, g, 0,
+                        id0, pol_kv);
+            tma_load_4d(kdst + Cfg::kKVBytes + sb * Cfg::kSubBytes, &tmap_v8, &bars->kv_full[st],
+                        sb * 64, g, 0, id0, pol_kv);
+          }
+        }
+      } else if (lane < 8) {
         uint8_t* kdst = smem + Cfg::kOffKV + st * 2 * Cfg::kKVBytes + lane * 2048;
         uint8_t* vdst = kdst + Cfg::kKVBytes;
 #pragma unroll
@@ -459,7 +478,7 @@ int launch_tc(void* out, const void* q, int64_t q_stride, const void* k_cache, c
   const int group = H / Kh;
   const int tq = Cfg::kBM / group;
   const uint64_t es = sizeof(T);
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mk8, mv8;
   {
     const uint64_t dims[3] = {uint64_t(D), uint64_t(H), uint64_t(total_q)};
     const uint64_t strides[2] = {uint64_t(D) * es, uint64_t(q_stride) * es};
@@ -479,15 +498,24 @@ int launch_tc(void* out, const void* q, int64_t q_stride, const void* k_cache, c
     rc = encode_tensor_map(&mv, tmap_dtype<T>(), 4, const_cast<void*>(v_cache), dims, strides,
                            box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    // 8 consecutive blocks of one KV head: 128 rows of 128 B, the same shared-memory
+    // image as 8 single-block boxes 2 KB apart
+    const uint32_t box8[4] = {64, 1, uint32_t(kBS), num_blocks >= 8 ? 8u : 1u};
+    rc = encode_tensor_map(&mk8, tmap_dtype<T>(), 4, const_cast<void*>(k_cache), dims, strides,
+                           box8, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_tensor_map(&mv8, tmap_dtype<T>(), 4, const_cast<void*>(v_cache), dims, strides,
+                           box8, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
   auto kern = prefill_tc_kernel<T, D>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   const int ntiles = (max_seqlen_q + tq - 1) / tq;
   dim3 grid(ntiles, Kh, R);
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
-      mq, mk, mv, static_cast<T*>(out),
+      mq, mk, mv, mk8, mv8, static_cast<T*>(out),
       bt, bt_stride, cu, lk, H, group, num_blocks, max_blocks,
-      scale * kLog2e, device_status_ptr());
+      scale * kLog2e, num_blocks >= 8 ? 1 : 0, device_status_ptr());
   return check_launch("as_varlen_prefill_attention (tcgen05)");
 }
 

@@ -324,6 +324,34 @@ def test_prefill_long_prefix_bf16():
     status_ok()
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_consecutive_block_runs(D):
+    """Tables whose 8-block KV tiles are runs of consecutive pool ids (loaded as one
+    16-block box) mixed with broken runs and a run ending at the last pool block."""
+    H, Kh = 32, 8
+    num_cached = [300, 1000, 200, 0]
+    num_new = [100, 64, 57, 90]
+    lens = [c + n for c, n in zip(num_cached, num_new)]
+    nb = [(L + 15) // 16 for L in lens]
+    NB = sum(nb) + 3
+    g = torch.Generator().manual_seed(40 + D)
+    tables, off = [], 3  # runs start at an id that is not a multiple of 8
+    for n in nb:
+        tables.append(list(range(off, off + n)))
+        off += n
+    tables[1][20], tables[1][21] = tables[1][21], tables[1][20]  # one broken run
+    tables[3] = list(range(NB - nb[3], NB))  # last run ends at the pool's last block
+    tables[2] = [0, 1, 2] + tables[2][3:]    # blocks 0-2 replace its first ids
+    kp = torch.randn(NB, 16, Kh, D, generator=g).to(torch.bfloat16)
+    vp = torch.randn(NB, 16, Kh, D, generator=g).to(torch.bfloat16)
+    q = torch.randn(sum(num_new), H, D, generator=g).to(torch.bfloat16)
+    cu = np.concatenate([[0], np.cumsum(num_new)]).astype(np.int32)
+    out = run_prefill(tables, kp, vp, q, cu, lens)
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
 # ---------------------------------------------------------------- block copy
 def test_block_copy_gather_and_seed_bit_exact():
     g = torch.Generator().manual_seed(6)
