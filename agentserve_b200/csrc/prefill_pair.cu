@@ -1,0 +1,556 @@
+// (4) Varlen prefill attention, head_dim 64: two query tiles per CTA sharing every
+// K/V tile, P kept in tensor memory.
+//
+// Semantics as in prefill_tcgen05.cu (LlamaAttention.forward over a cached prefix,
+// agentserve/model/llama.py:128-186): token i of a sequence with P cached tokens
+// attends to keys 0..P+i, K/V read in place from the paged pool.
+//
+// CTA = (pair of query tiles, KV head g, sequence).  Query tile i (i = 0, 1) holds
+// 128 rows = tq tokens x the `group` query heads of KV head g.  Per KV tile of 128
+// keys (8 paged blocks) the K and V boxes land in shared memory once and feed both
+// query tiles, halving TMA work and shared-memory traffic per query row compared
+// with one tile per CTA.  Warp roles (320 threads, one CTA per SM):
+//   warp 0      TMA producer: both Q tiles once, then K/V tiles into a 4-stage ring;
+//   warp 1      MMA issuer (one thread), polling: S_i = Q_i K^T (both operands from
+//               shared memory, 128B swizzle) as soon as tile j's K/V is in and
+//               softmax i has read S_i(j-1); O_i += P_i V with P_i read from TMEM
+//               as soon as softmax i has written it;
+//   warps 2-5   softmax of query tile 0, warps 6-9 softmax of query tile 1: one TMEM
+//               lane (row) per thread; online softmax in the exp2 domain with a lazy
+//               maximum (O rescaled in TMEM only when a row maximum grows by > 2^8),
+//               paired fp32 arithmetic (f32x2) and 3-input max; P packed to 16-bit
+//               pairs and stored to TMEM with tcgen05.st.  The two warps that share an
+//               SM sub-partition take turns on its exponent unit (ping-pong), so one
+//               warp's TMEM loads, stores and waits overlap the other's exponentials.
+// TMEM (512 columns): tile i owns [256 i, 256 i + 256): S 128 columns, P 64 columns
+// (128 keys as 16-bit pairs), O 64 columns.  Every wait is bounded; a wait that
+// runs out sets status bit 4, the CTA stops issuing, drains its MMAs, frees TMEM
+// and writes nothing.
+#include <type_traits>
+
+#include "common.cuh"
+#include "host_util.h"
+#include "prefill_tcgen05.h"
+#include "tcgen05.cuh"
+
+namespace asb {
+namespace {
+
+constexpr int kBS = 16;
+constexpr float kLazySlack = 8.0f;
+
+#ifndef AS_PREFILL_PAIR_STAGES
+#define AS_PREFILL_PAIR_STAGES 4
+#endif
+#ifndef AS_PREFILL_PINGPONG
+#define AS_PREFILL_PINGPONG 1
+#endif
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic) --------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+struct PairCfg {
+  static constexpr int D = 64;
+  static constexpr int kBM = 128;
+  static constexpr int kBN = 128;
+  static constexpr int kStages = AS_PREFILL_PAIR_STAGES;
+  static constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 B (64 16-bit elements)
+  static constexpr int kOffQ = 0;               // Q tile i at kOffQ + i * kTileBytes
+  static constexpr int kOffKV = 2 * kTileBytes;  // stage s: K at +2s*kTileBytes, V after it
+  static constexpr int kOffBar = kOffKV + kStages * 2 * kTileBytes;
+  static constexpr int kSmemBytes = kOffBar + 512;
+  static constexpr int kThreads = 320;
+  static constexpr int kTmemCols = 512;
+};
+
+struct PairBars {
+  uint64_t q_full;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint64_t s_full[2];
+  uint64_t s_free[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint64_t turn[2][4];  // exponent-phase hand-off between the two warps sharing an SM sub-partition
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+static_assert(sizeof(PairBars) <= 512, "barrier block exceeds its shared-memory slot");
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* p) {
+  uint4 v;
+  v.x = pack2<T>(p[0], p[1]);
+  v.y = pack2<T>(p[2], p[3]);
+  v.z = pack2<T>(p[4], p[5]);
+  v.w = pack2<T>(p[6], p[7]);
+  return v;
+}
+
+__device__ __forceinline__ bool aborted(volatile int* f) { return *f != 0; }
+
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                    const __grid_constant__ CUtensorMap tmap_k,
+                    const __grid_constant__ CUtensorMap tmap_v,
+                    const __grid_constant__ CUtensorMap tmap_k8,
+                    const __grid_constant__ CUtensorMap tmap_v8, T* __restrict__ out,
+                    const int32_t* __restrict__ bt, int64_t bt_stride,
+                    const int32_t* __restrict__ cu_seqlens_q,
+                    const int32_t* __restrict__ seq_lens_k, int H, int group, int num_blocks,
+                    int max_blocks, float scale_log2, int run8_ok, int* status) {
+  using Cfg = PairCfg;
+  constexpr int D = Cfg::D;
+  constexpr int NS = Cfg::kStages;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = tc::idesc_f16(kBF16, 128, 128, false, false);
+  constexpr uint32_t kIdescO = tc::idesc_f16(kBF16, 128, D, false, true);
+
+  const int r = blockIdx.z;
+  const int g = blockIdx.y;
+  const int q_begin = cu_seqlens_q[r];
+  const int nq = cu_seqlens_q[r + 1] - q_begin;
+  const int tq = Cfg::kBM / group;
+  const int pair = int(gridDim.x) - 1 - int(blockIdx.x);  // longest (last) pairs first
+  const int t0 = pair * 2 * tq;
+  if (t0 >= nq) return;
+  int Lk = seq_lens_k[r];
+  if (Lk > max_blocks * kBS) {
+    if (threadIdx.x == 0) flag_status(status, kStatusBadLength);
+    Lk = max_blocks * kBS;
+  }
+  const int P = Lk - nq;
+  if (P < 0) {
+    if (threadIdx.x == 0) flag_status(status, kStatusBadLength);
+    return;
+  }
+  const bool two = t0 + tq < nq;  // query tile 1 holds at least one token
+  // KV tiles each query tile attends to (causal: tile 1 may need one more)
+  const int n_kv0 = (P + min(t0 + tq, nq) + Cfg::kBN - 1) / Cfg::kBN;
+  const int n_kv1 = two ? (P + min(t0 + 2 * tq, nq) + Cfg::kBN - 1) / Cfg::kBN : 0;
+  const int n_kv = two ? n_kv1 : n_kv0;
+  const int nblk_seq = (Lk + kBS - 1) / kBS;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) flag_status(status, kStatusWaitTimeout);
+    return;
+  }
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + Cfg::kOffBar);
+  volatile int* abort_flag = &bars->abort;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->s_free[i], 4);
+      mbar_init(&bars->p_full[i], 4);
+      mbar_init(&bars->pv_done[i], 1);
+      for (int q = 0; q < 4; ++q) mbar_init(&bars->turn[i][q], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t sQ = smem_u32(smem + Cfg::kOffQ);
+  const uint32_t sKV = smem_u32(smem + Cfg::kOffKV);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    const int filler = (nblk_seq > 0) ? bt[int64_t(r) * bt_stride] : 0;
+    const int fill_ok = (filler >= 0 && filler < num_blocks) ? filler : 0;
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      tma_prefetch_desc(&tmap_k8);
+      tma_prefetch_desc(&tmap_v8);
+      mbar_arrive_expect_tx(&bars->q_full, (two ? 2 : 1) * Cfg::kTileBytes);
+      const uint64_t pol_q = l2_policy_evict_first();
+      tma_load_3d(smem + Cfg::kOffQ, &tmap_q, &bars->q_full, 0, g * group, q_begin + t0, pol_q);
+      if (two)
+        tma_load_3d(smem + Cfg::kOffQ + Cfg::kTileBytes, &tmap_q, &bars->q_full, 0, g * group,
+                    q_begin + t0 + tq, pol_q);
+    }
+    auto load_id = [&](int jt) -> int {
+      const int blk = 8 * jt + (lane & 7);
+      int id = fill_ok;  // keys past the sequence: finite filler data, masked to p = 0
+      if (blk < nblk_seq) {
+        id = __ldg(bt + int64_t(r) * bt_stride + blk);
+        if (id < 0 || id >= num_blocks) {
+          flag_status(status, kStatusBadBlockId);
+          id = fill_ok;
+        }
+      }
+      return id;
+    };
+    const uint64_t pol_kv = l2_policy_evict_last();
+    int id_next = load_id(0);
+    for (int j = 0; j < n_kv; ++j) {
+      if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
+      const int st = j % NS;
+      const bool ready = j < NS || mbar_wait(&bars->kv_empty[st], ((j / NS) + 1) & 1, status);
+      if (!__all_sync(0xffffffffu, ready)) {
+        *abort_flag = 1;
+        break;
+      }
+      const int id = id_next;
+      if (j + 1 < n_kv) id_next = load_id(j + 1);
+      const int id0 = __shfl_sync(0xffffffffu, id, 0);
+      const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & 7));
+      if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kTileBytes);
+      __syncwarp();
+      uint8_t* kst = smem + Cfg::kOffKV + st * 2 * Cfg::kTileBytes;
+      if (run8) {
+        if (lane == 0) {
+          tma_load_4d(kst, &tmap_k8, &bars->kv_full[st], 0, g, 0, id0, pol_kv);
+          tma_load_4d(kst + Cfg::kTileBytes, &tmap_v8, &bars->kv_full[st], 0, g, 0, id0, pol_kv);
+        }
+      } else if (lane < 8) {
+        tma_load_4d(kst + lane * 2048, &tmap_k, &bars->kv_full[st], 0, g, 0, id, pol_kv);
+        tma_load_4d(kst + Cfg::kTileBytes + lane * 2048, &tmap_v, &bars->kv_full[st], 0, g, 0,
+                    id, pol_kv);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int nk[2] = {n_kv0, n_kv1};
+      auto issue_s = [&](int i, int st) {
+        const uint32_t q = sQ + i * Cfg::kTileBytes;
+        const uint32_t k = sKV + st * 2 * Cfg::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_f16(tmem + 256 * i, tc::sdesc_sw128(q + kk * 32, 16, 1024),
+                      tc::sdesc_sw128(k + kk * 32, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+      };
+      auto issue_pv = [&](int i, int st, bool acc) {
+        const uint32_t v = sKV + st * 2 * Cfg::kTileBytes + Cfg::kTileBytes;
+        const uint32_t tP = tmem + 256 * i + 128;
+        const uint32_t tO = tmem + 256 * i + 192;
+#pragma unroll
+        for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
+          tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kTileBytes, 1024),
+                         kIdescO, (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars->q_full, 0, status);
+      int js[2] = {0, 0};  // next S tile per query tile
+      int jp[2] = {0, 0};  // next PV tile per query tile
+      uint64_t t_last = global_timer_ns();
+      uint32_t spin = 0;
+      while (ok && (jp[0] < nk[0] || jp[1] < nk[1])) {
+        if (aborted(abort_flag)) break;
+        bool did = false;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int j = js[i];
+          if (j < nk[i] && mbar_try_wait(&bars->kv_full[j % NS], (j / NS) & 1) &&
+              (j == 0 || mbar_try_wait(&bars->s_free[i], (j - 1) & 1))) {
+            tc::fence_after_sync();
+            issue_s(i, j % NS);
+            tc::commit(&bars->s_full[i]);
+            js[i] = j + 1;
+            did = true;
+          }
+          const int jq = jp[i];
+          if (jq < js[i] && mbar_try_wait(&bars->p_full[i], jq & 1)) {
+            tc::fence_after_sync();
+            issue_pv(i, jq % NS, jq > 0);
+            tc::commit(&bars->pv_done[i]);
+            jp[i] = jq + 1;
+            did = true;
+            // the stage is free once every query tile that reads it has issued PV
+            const int o = 1 - i;
+            if (jp[o] > jq || jq >= nk[o]) tc::commit(&bars->kv_empty[jq % NS]);
+          }
+        }
+        if (did) {
+          t_last = global_timer_ns();
+        } else if ((++spin & 255u) == 0u && global_timer_ns() - t_last > kWaitLimitNs) {
+          flag_status(status, kStatusWaitTimeout);
+          ok = false;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      tc::commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int i = (warp - 2) >> 2;  // query tile
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int t = row / group;
+    const int hq = row - t * group;
+    const int ti0 = t0 + i * tq;    // first token of this query tile
+    const int tok = ti0 + t;
+    const bool valid = tok < nq;
+    const int qpos = valid ? P + tok : P + ti0;
+    const uint32_t trow = uint32_t(quad * 32) << 16;
+    const uint32_t tS = tmem + 256 * i + trow;
+    const uint32_t tP = tS + 128;
+    const uint32_t tO = tS + 192;
+    const int nkv = i ? n_kv1 : n_kv0;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const bool go = !aborted(abort_flag) && mbar_wait(&bars->s_full[i], j & 1, status);
+      if (!__all_sync(0xffffffffu, go)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float x[128];
+      {
+        uint32_t v0[32], v1[32], v2[32], v3[32];
+        tc::ld_32x32b_x32(tS + 0, v0);
+        tc::ld_32x32b_x32(tS + 32, v1);
+        tc::ld_32x32b_x32(tS + 64, v2);
+        tc::ld_32x32b_x32(tS + 96, v3);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          x[c] = __uint_as_float(v0[c]);
+          x[32 + c] = __uint_as_float(v1[c]);
+          x[64 + c] = __uint_as_float(v2[c]);
+          x[96 + c] = __uint_as_float(v3[c]);
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_free[i]);  // S(j+1) may overwrite S now
+
+      const int lim = qpos - j * Cfg::kBN;  // keys c <= lim are visible
+      if (lim < Cfg::kBN - 1) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
+      }
+      float mp[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mp[c] = fmaxf(x[c], x[8 + c]);
+#pragma unroll
+      for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mp[e] = max3f(mp[e], x[c + e], x[c + 8 + e]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      float alpha = 1.f;
+      if (mx * scale_log2 > m + kLazySlack) {
+        const float m_new = mx * scale_log2;
+        alpha = fast_exp2(m - m_new);
+        m = m_new;
+      }
+      const float neg_m = -m;
+      // Warp q of group 0 and warp q of group 1 run on the same SM sub-partition and
+      // share its exponent unit: they take turns (tile j of group 0, tile j of group 1,
+      // tile j+1 of group 0, ...), so one warp's TMEM traffic and waits overlap the
+      // other's exponentials instead of both stalling together.  A warp waits only
+      // for a hand-off its partner will make.
+      const bool wait_turn = AS_PREFILL_PINGPONG && (i == 0 ? (j >= 1 && j - 1 < n_kv1) : (j < n_kv0));
+      if (wait_turn) {
+        const uint32_t par = (i == 0 ? (j - 1) : j) & 1;
+        if (!__all_sync(0xffffffffu, !aborted(abort_flag) && mbar_wait(&bars->turn[i][quad], par, status))) {
+          ok = false;
+          break;
+        }
+      }
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = f2_pack(neg_m, neg_m);
+      uint64_t sp2[4] = {0, 0, 0, 0};  // 8 independent fp32 partial sums, as pairs
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const uint64_t xs = f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2);
+        float a, b;
+        f2_unpack(xs, a, b);
+        const uint64_t p2 = f2_pack(fast_exp2(a), fast_exp2(b));
+        sp2[c & 3] = f2_add(sp2[c & 3], p2);
+        float p0, p1;
+        f2_unpack(p2, p0, p1);
+        pk[c] = pack2<T>(p0, p1);
+      }
+      float sum;
+      {
+        const uint64_t s01 = f2_add(f2_add(sp2[0], sp2[1]), f2_add(sp2[2], sp2[3]));
+        float a, b;
+        f2_unpack(s01, a, b);
+        sum = a + b;
+      }
+      if (AS_PREFILL_PINGPONG) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
+      }
+      if (j > 0) {  // PV(j-1) still reads P and accumulates into O
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (j - 1) & 1, status))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+      }
+      tc::st_32x32b_x32(tP, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      tc::st_32x32b_x32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+      l = l * alpha + sum;
+      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(tO + c * 32, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tc::st_32x32b_x32(tO + c * 32, o);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[i]);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool done = ok && nkv > 0 &&
+                      __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (nkv - 1) & 1, status));
+    if (done) {
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* dst = out + (int64_t(q_begin) + tok) * int64_t(H) * D + int64_t(g * group + hq) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tc::ld_32x32b_x32(tO + c * 32, o);
+        tc::wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            float f[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) f[u] = __uint_as_float(o[e + u]) * inv;
+            *reinterpret_cast<uint4*>(dst + c * 32 + e) = pack8<T>(f);
+          }
+        }
+      }
+    } else if (ok && nkv > 0) {
+      *abort_flag = 1;
+    }
+    tc::fence_before_sync();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+template <typename T>
+CUtensorMapDataType tmap_dtype() {
+  return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <typename T>
+int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                const void* v_cache, const int32_t* bt, int64_t bt_stride, const int32_t* cu,
+                const int32_t* lk, int R, int max_seqlen_q, int total_q, int H, int Kh,
+                int num_blocks, int max_blocks, float scale, cudaStream_t stream) {
+  using Cfg = PairCfg;
+  constexpr int D = Cfg::D;
+  const int group = H / Kh;
+  const int tq = Cfg::kBM / group;
+  const uint64_t es = sizeof(T);
+  CUtensorMap mq, mk, mv, mk8, mv8;
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(H), uint64_t(total_q)};
+    const uint64_t strides[2] = {uint64_t(D) * es, uint64_t(q_stride) * es};
+    const uint32_t box[3] = {64, uint32_t(group), uint32_t(tq)};
+    int rc = encode_tensor_map(&mq, tmap_dtype<T>(), 3, const_cast<void*>(q), dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[4] = {uint64_t(D), uint64_t(Kh), uint64_t(kBS), uint64_t(num_blocks)};
+    const uint64_t strides[3] = {uint64_t(D) * es, uint64_t(Kh) * D * es,
+                                 uint64_t(kBS) * Kh * D * es};
+    const uint32_t box[4] = {64, 1, uint32_t(kBS), 1};
+    const uint32_t box8[4] = {64, 1, uint32_t(kBS), num_blocks >= 8 ? 8u : 1u};
+    int rc = encode_tensor_map(&mk, tmap_dtype<T>(), 4, const_cast<void*>(k_cache), dims, strides,
+                               box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+      rc = encode_tensor_map(&mv, tmap_dtype<T>(), 4, const_cast<void*>(v_cache), dims, strides,
+                             box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+      rc = encode_tensor_map(&mk8, tmap_dtype<T>(), 4, const_cast<void*>(k_cache), dims, strides,
+                             box8, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+      rc = encode_tensor_map(&mv8, tmap_dtype<T>(), 4, const_cast<void*>(v_cache), dims, strides,
+                             box8, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  auto kern = prefill_pair_kernel<T>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  const int npairs = (max_seqlen_q + 2 * tq - 1) / (2 * tq);
+  dim3 grid(npairs, Kh, R);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
+      mq, mk, mv, mk8, mv8, static_cast<T*>(out), bt, bt_stride, cu, lk, H, group, num_blocks,
+      max_blocks, scale * kLog2e, num_blocks >= 8 ? 1 : 0, device_status_ptr());
+  return check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
+}
+
+}  // namespace
+
+int prefill_pair_launch(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                        const void* v_cache, const int32_t* bt, int64_t bt_stride,
+                        const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int R,
+                        int max_seqlen_q, int total_q, int H, int Kh, int num_blocks,
+                        int max_blocks, float scale, int dtype, cudaStream_t stream) {
+  if (dtype == AS_DTYPE_BF16)
+    return launch_pair<__nv_bfloat16>(out, q, q_stride, k_cache, v_cache, bt, bt_stride,
+                                      cu_seqlens_q, seq_lens_k, R, max_seqlen_q, total_q, H, Kh,
+                                      num_blocks, max_blocks, scale, stream);
+  return launch_pair<__half>(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
+                             seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks, max_blocks,
+                             scale, stream);
+}
+
+}  // namespace asb
