@@ -109,6 +109,59 @@ class DeviceBlockAllocator:
         if row is not None:
             self._free_rows.append(row)
 
+    # ------------------------------------------------------------------ prefix sharing
+    def _check_live(self, block_ids: Sequence[int]) -> List[int]:
+        ids = [int(b) for b in block_ids]
+        for b in ids:
+            if not (0 <= b < self.num_blocks) or self._ref[b] <= 0:
+                raise ValueError(f"block {b} is not allocated")
+        return ids
+
+    def retain_blocks(self, block_ids: Sequence[int]) -> None:
+        """Take a reference on live blocks (a prefix-cache entry keeping a finished
+        request's prefix blocks), using the reference's per-block ref count
+        (Block.ref_count, cache.py:24-30)."""
+        for b in self._check_live(block_ids):
+            self._ref[b] += 1
+
+    def release_blocks(self, block_ids: Sequence[int]) -> None:
+        """Drop references taken by retain_blocks; a block whose count reaches zero
+        returns to the free list (in this order, like free())."""
+        for b in self._check_live(block_ids):
+            self._ref[b] -= 1
+            if self._ref[b] == 0:
+                self._used.discard(b)
+                self._free.append(b)
+
+    def share_blocks(self, request_id: str, block_ids: Sequence[int]) -> None:
+        """Zero-copy prefix hit: the request's block list (and its device table row)
+        starts with these live blocks, shared with their other holders, instead of a
+        fresh copy of their K/V (engine.py:274-281 seeds a clone).  Shared blocks are
+        read in place by the attention kernels; new tokens must land in blocks of the
+        request's own, so share only full blocks (a block-aligned prefix match, as
+        prefix_cache.py:110-183 makes) and allocate() the rest afterwards."""
+        ids = self._check_live(block_ids)
+        if self._request_blocks.get(request_id):
+            raise ValueError(f"request {request_id} already holds blocks; share the prefix first")
+        if len(ids) > self.max_blocks_per_seq:
+            raise MemoryError(f"request {request_id} would hold {len(ids)} blocks; "
+                              f"the device table row holds {self.max_blocks_per_seq}")
+        row = self._rows.get(request_id)
+        if row is None:
+            if not self._free_rows:
+                raise MemoryError(f"no free block-table row (max_seqs={self.max_seqs})")
+            row = self._free_rows.popleft()
+            self._rows[request_id] = row
+        for b in ids:
+            self._ref[b] += 1
+        self._request_blocks[request_id] = list(ids)
+        if ids:
+            self.block_tables[row, :len(ids)].copy_(self._host_ints(ids, torch.int32),
+                                                    non_blocking=True)
+
+    def ref_count(self, block_id: int) -> int:
+        return self._ref[block_id]
+
     def blocks_for(self, request_id: str) -> List[int]:
         return list(self._request_blocks.get(request_id, []))
 

@@ -146,22 +146,27 @@ int launch_prefill_generic(void* out, const void* q, int64_t q_stride, const voi
 
 using namespace asb;
 
-extern "C" int as_varlen_prefill_attention(void* out, const void* q, int64_t q_stride,
-                                           const void* k_cache, const void* v_cache,
-                                           const int32_t* block_tables, int64_t bt_stride,
-                                           const int32_t* cu_seqlens_q, const int32_t* seq_lens_k,
-                                           int32_t num_seqs, int32_t max_seqlen_q,
-                                           int32_t total_q, int32_t num_heads,
-                                           int32_t num_kv_heads, int32_t head_dim,
-                                           int32_t block_size, int32_t num_blocks,
-                                           int32_t max_blocks, float scale, int32_t dtype,
-                                           as_stream_t stream) {
+namespace {
+
+// head_dim 64 on the tensor cores takes the query-tile-pair kernel, which can split KV
+bool pair_path(int32_t dtype, int32_t H, int32_t Kh, int32_t D, const void* q, int64_t q_stride,
+               const void* k_cache, const void* v_cache, const void* out) {
+  return D == 64 && prefill_tc_supported(dtype, H, Kh, D, q, q_stride, k_cache, v_cache, out);
+}
+
+int prefill_entry(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                  const void* v_cache, const int32_t* block_tables, int64_t bt_stride,
+                  const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int32_t num_seqs,
+                  int32_t max_seqlen_q, int32_t total_q, int32_t num_heads, int32_t num_kv_heads,
+                  int32_t head_dim, int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                  float scale, int32_t dtype, int32_t num_splits, void* workspace,
+                  size_t workspace_bytes, as_stream_t stream) {
   if (!dtype_size(dtype)) return fail(AS_ERR_INVALID_ARG, "as_varlen_prefill_attention: unknown dtype");
   if (block_size != kBlockSize)
     return fail(AS_ERR_UNSUPPORTED, "as_varlen_prefill_attention: block_size must be 16");
   if (num_seqs < 0 || total_q < 0 || num_heads <= 0 || num_kv_heads <= 0 ||
       num_heads % num_kv_heads || head_dim <= 0 || head_dim > 256 || num_blocks <= 0 ||
-      max_blocks <= 0 || bt_stride < max_blocks || max_seqlen_q < 0)
+      max_blocks <= 0 || bt_stride < max_blocks || max_seqlen_q < 0 || num_splits < 0)
     return fail(AS_ERR_INVALID_ARG, "as_varlen_prefill_attention: bad sizes");
   if (num_seqs == 0 || total_q == 0) return AS_OK;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !cu_seqlens_q || !seq_lens_k)
@@ -173,9 +178,26 @@ extern "C" int as_varlen_prefill_attention(void* out, const void* q, int64_t q_s
 
   if (prefill_tc_supported(dtype, num_heads, num_kv_heads, head_dim, q, q_stride, k_cache,
                            v_cache, out)) {
+    int n_split = 1;
+    if (pair_path(dtype, num_heads, num_kv_heads, head_dim, q, q_stride, k_cache, v_cache, out) &&
+        num_splits != 1) {
+      n_split = prefill_pair_splits(num_seqs, max_seqlen_q, num_heads, num_kv_heads, max_blocks,
+                                    num_splits);
+      const size_t need = prefill_pair_workspace_size(num_seqs, max_seqlen_q, num_heads,
+                                                      num_kv_heads, n_split);
+      if (need > 0 && (!workspace || workspace_bytes < need)) {
+        if (num_splits > 1)
+          return fail(AS_ERR_WORKSPACE, "as_varlen_prefill_attention: workspace of %zu bytes < %zu",
+                      workspace_bytes, need);
+        n_split = 1;  // automatic split: fall back to one CTA per pair
+      }
+      if (n_split > 1 && (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(AS_ERR_INVALID_ARG, "as_varlen_prefill_attention: workspace not 256-byte aligned");
+    }
     return prefill_tc_launch(out, q, q_stride, k_cache, v_cache, block_tables, bt_stride,
                              cu_seqlens_q, seq_lens_k, num_seqs, max_seqlen_q, total_q, num_heads,
-                             num_kv_heads, head_dim, num_blocks, max_blocks, scale, dtype, s);
+                             num_kv_heads, head_dim, num_blocks, max_blocks, scale, dtype, n_split,
+                             workspace, s);
   }
   switch (dtype) {
     case AS_DTYPE_F32:
@@ -195,4 +217,51 @@ extern "C" int as_varlen_prefill_attention(void* out, const void* q, int64_t q_s
                                                    num_kv_heads, head_dim, num_blocks, max_blocks,
                                                    scale, s);
   }
+}
+
+}  // namespace
+
+extern "C" int as_varlen_prefill_attention(void* out, const void* q, int64_t q_stride,
+                                           const void* k_cache, const void* v_cache,
+                                           const int32_t* block_tables, int64_t bt_stride,
+                                           const int32_t* cu_seqlens_q, const int32_t* seq_lens_k,
+                                           int32_t num_seqs, int32_t max_seqlen_q,
+                                           int32_t total_q, int32_t num_heads,
+                                           int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t block_size, int32_t num_blocks,
+                                           int32_t max_blocks, float scale, int32_t dtype,
+                                           as_stream_t stream) {
+  return prefill_entry(out, q, q_stride, k_cache, v_cache, block_tables, bt_stride, cu_seqlens_q,
+                       seq_lens_k, num_seqs, max_seqlen_q, total_q, num_heads, num_kv_heads,
+                       head_dim, block_size, num_blocks, max_blocks, scale, dtype, 1, nullptr, 0,
+                       stream);
+}
+
+extern "C" int as_varlen_prefill_attention_ws(
+    void* out, const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+    const int32_t* block_tables, int64_t bt_stride, const int32_t* cu_seqlens_q,
+    const int32_t* seq_lens_k, int32_t num_seqs, int32_t max_seqlen_q, int32_t total_q,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t num_blocks, int32_t max_blocks, float scale, int32_t dtype, int32_t num_splits,
+    void* workspace, size_t workspace_bytes, as_stream_t stream) {
+  return prefill_entry(out, q, q_stride, k_cache, v_cache, block_tables, bt_stride, cu_seqlens_q,
+                       seq_lens_k, num_seqs, max_seqlen_q, total_q, num_heads, num_kv_heads,
+                       head_dim, block_size, num_blocks, max_blocks, scale, dtype, num_splits,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t as_varlen_prefill_workspace_size(int32_t num_seqs, int32_t max_seqlen_q,
+                                                   int32_t num_heads, int32_t num_kv_heads,
+                                                   int32_t head_dim, int32_t max_blocks,
+                                                   int32_t num_splits, int32_t dtype) {
+  if (num_seqs <= 0 || max_seqlen_q <= 0 || num_heads <= 0 || num_kv_heads <= 0 ||
+      num_heads % num_kv_heads || max_blocks <= 0 || num_splits == 1 || num_splits < 0)
+    return 0;
+  const int group = num_heads / num_kv_heads;
+  if (head_dim != 64 || (dtype != AS_DTYPE_BF16 && dtype != AS_DTYPE_F16) || group > 128 ||
+      128 % group)
+    return 0;
+  const int n = prefill_pair_splits(num_seqs, max_seqlen_q, num_heads, num_kv_heads, max_blocks,
+                                    num_splits);
+  return prefill_pair_workspace_size(num_seqs, max_seqlen_q, num_heads, num_kv_heads, n);
 }

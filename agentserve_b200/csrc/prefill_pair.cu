@@ -38,6 +38,14 @@ namespace {
 
 constexpr int kBS = 16;
 constexpr float kLazySlack = 8.0f;
+constexpr int kMaxSplits = 16;
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+// query-tile pairs per (sequence, KV head): 2 x 128 rows = 2 x (128 / group) tokens
+int pair_count(int max_seqlen_q, int H, int Kh) {
+  const int tq = 128 / (H / Kh);
+  return (max_seqlen_q + 2 * tq - 1) / (2 * tq);
+}
 
 #ifndef AS_PREFILL_PAIR_STAGES
 #define AS_PREFILL_PAIR_STAGES 4
@@ -122,7 +130,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const int32_t* __restrict__ bt, int64_t bt_stride,
                     const int32_t* __restrict__ cu_seqlens_q,
                     const int32_t* __restrict__ seq_lens_k, int H, int group, int num_blocks,
-                    int max_blocks, float scale_log2, int run8_ok, int* status) {
+                    int max_blocks, float scale_log2, int run8_ok, int n_split,
+                    float* __restrict__ part_o, float2* __restrict__ part_ml, int* status) {
   using Cfg = PairCfg;
   constexpr int D = Cfg::D;
   constexpr int NS = Cfg::kStages;
@@ -135,7 +144,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int q_begin = cu_seqlens_q[r];
   const int nq = cu_seqlens_q[r + 1] - q_begin;
   const int tq = Cfg::kBM / group;
-  const int pair = int(gridDim.x) - 1 - int(blockIdx.x);  // longest (last) pairs first
+  // x = pair * n_split + split, pairs in reverse order (longest, last pairs first)
+  const int npairs = int(gridDim.x) / n_split;
+  const int pair = npairs - 1 - int(blockIdx.x) / n_split;
+  const int split = int(blockIdx.x) % n_split;
   const int t0 = pair * 2 * tq;
   if (t0 >= nq) return;
   int Lk = seq_lens_k[r];
@@ -153,6 +165,13 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int n_kv0 = (P + min(t0 + tq, nq) + Cfg::kBN - 1) / Cfg::kBN;
   const int n_kv1 = two ? (P + min(t0 + 2 * tq, nq) + Cfg::kBN - 1) / Cfg::kBN : 0;
   const int n_kv = two ? n_kv1 : n_kv0;
+  // This CTA's share of the KV tiles (split-KV): [j0, j1); query tile i attends to
+  // cnt_i of them (tile 0 may end earlier under the causal mask).
+  const int j0 = int(int64_t(split) * n_kv / n_split);
+  const int j1 = int(int64_t(split + 1) * n_kv / n_split);
+  const int cnt0 = max(0, min(j1, n_kv0) - j0);
+  const int cnt1 = two ? max(0, min(j1, n_kv1) - j0) : 0;
+  const int n_load = max(cnt0, cnt1);
   const int nblk_seq = (Lk + kBS - 1) / kBS;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -224,8 +243,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       return id;
     };
     const uint64_t pol_kv = l2_policy_evict_last();
-    int id_next = load_id(0);
-    for (int j = 0; j < n_kv; ++j) {
+    int id_next = load_id(j0);
+    for (int j = 0; j < n_load; ++j) {  // local tile index; global tile j0 + j
       if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
       const int st = j % NS;
       const bool ready = j < NS || mbar_wait(&bars->kv_empty[st], ((j / NS) + 1) & 1, status);
@@ -234,7 +253,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         break;
       }
       const int id = id_next;
-      if (j + 1 < n_kv) id_next = load_id(j + 1);
+      if (j + 1 < n_load) id_next = load_id(j0 + j + 1);
       const int id0 = __shfl_sync(0xffffffffu, id, 0);
       const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & 7));
       if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kTileBytes);
@@ -255,7 +274,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const int nk[2] = {n_kv0, n_kv1};
+      const int nk[2] = {cnt0, cnt1};  // local tile counts
       auto issue_s = [&](int i, int st) {
         const uint32_t q = sQ + i * Cfg::kTileBytes;
         const uint32_t k = sKV + st * 2 * Cfg::kTileBytes;
@@ -331,10 +350,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const uint32_t tS = tmem + 256 * i + trow;
     const uint32_t tP = tS + 128;
     const uint32_t tO = tS + 192;
-    const int nkv = i ? n_kv1 : n_kv0;
+    const int nkv = i ? cnt1 : cnt0;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    for (int j = 0; j < nkv; ++j) {  // local tile index; global tile j0 + j
       const bool go = !aborted(abort_flag) && mbar_wait(&bars->s_full[i], j & 1, status);
       if (!__all_sync(0xffffffffu, go)) {
         ok = false;
@@ -361,7 +380,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_free[i]);  // S(j+1) may overwrite S now
 
-      const int lim = qpos - j * Cfg::kBN;  // keys c <= lim are visible
+      const int lim = qpos - (j0 + j) * Cfg::kBN;  // keys c <= lim are visible
       if (lim < Cfg::kBN - 1) {
 #pragma unroll
         for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
@@ -382,13 +401,15 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         alpha = fast_exp2(m - m_new);
         m = m_new;
       }
-      const float neg_m = -m;
+      // A row whose keys in this split are all masked so far keeps m = -inf; its
+      // exponentials are then exp2(-inf) = 0 instead of NaN.
+      const float neg_m = m == -INFINITY ? 0.f : -m;
       // Warp q of group 0 and warp q of group 1 run on the same SM sub-partition and
       // share its exponent unit: they take turns (tile j of group 0, tile j of group 1,
       // tile j+1 of group 0, ...), so one warp's TMEM traffic and waits overlap the
       // other's exponentials instead of both stalling together.  A warp waits only
       // for a hand-off its partner will make.
-      const bool wait_turn = AS_PREFILL_PINGPONG && (i == 0 ? (j >= 1 && j - 1 < n_kv1) : (j < n_kv0));
+      const bool wait_turn = AS_PREFILL_PINGPONG && (i == 0 ? (j >= 1 && j - 1 < cnt1) : (j < cnt0));
       if (wait_turn) {
         const uint32_t par = (i == 0 ? (j - 1) : j) & 1;
         if (!__all_sync(0xffffffffu, !aborted(abort_flag) && mbar_wait(&bars->turn[i][quad], par, status))) {
@@ -451,7 +472,31 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (!ok) *abort_flag = 1;
     const bool done = ok && nkv > 0 &&
                       __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (nkv - 1) & 1, status));
-    if (done) {
+    if (n_split > 1) {
+      // split-KV partial: unnormalised O row, (m, l); merged by prefill_merge_kernel
+      const int64_t rec = ((int64_t(r) * gridDim.y + g) * npairs + pair) * n_split + split;
+      const int64_t prow = rec * 256 + i * 128 + row;
+      if (done) {
+        tc::fence_after_sync();
+        float* po = part_o + prow * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(tO + c * 32, o);
+          tc::wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<uint4*>(po + c * 32 + e) = make_uint4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+          }
+        }
+        if (valid) part_ml[prow] = make_float2(m, l);
+      } else if (ok && nkv == 0) {
+        if (valid) part_ml[prow] = make_float2(-INFINITY, 0.f);  // no keys in this split
+      } else if (ok) {
+        *abort_flag = 1;
+      }
+    } else if (done) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* dst = out + (int64_t(q_begin) + tok) * int64_t(H) * D + int64_t(g * group + hq) * D;
@@ -483,6 +528,53 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   }
 }
 
+// Combines the n_split partials of every (query-tile pair, KV head, sequence):
+// O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s.  One warp per row,
+// two head-dim columns per lane.  Units and rows the main kernel skipped are skipped.
+template <typename T>
+__global__ void __launch_bounds__(256)
+prefill_merge_kernel(T* __restrict__ out, const float* __restrict__ part_o,
+                     const float2* __restrict__ part_ml, const int32_t* __restrict__ cu_seqlens_q,
+                     const int32_t* __restrict__ seq_lens_k, int H, int group, int npairs,
+                     int n_split, int max_blocks) {
+  constexpr int D = PairCfg::D;
+  const int r = blockIdx.z, g = blockIdx.y, pair = blockIdx.x;
+  const int q_begin = cu_seqlens_q[r];
+  const int nq = cu_seqlens_q[r + 1] - q_begin;
+  const int tq = PairCfg::kBM / group;
+  const int t0 = pair * 2 * tq;
+  if (t0 >= nq) return;
+  const int Lk = min(seq_lens_k[r], max_blocks * kBS);
+  if (Lk - nq < 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rec0 = ((int64_t(r) * gridDim.y + g) * npairs + pair) * n_split;
+  for (int rr = warp; rr < 256; rr += 8) {
+    const int i = rr >> 7, row = rr & 127;
+    const int tok = t0 + i * tq + row / group;
+    if (tok >= nq) continue;
+    const int hq = row % group;
+    float M = -INFINITY;
+    for (int sp = 0; sp < n_split; ++sp) {
+      const float2 ml = part_ml[(rec0 + sp) * 256 + rr];
+      if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    float L = 0.f, ox = 0.f, oy = 0.f;
+    for (int sp = 0; sp < n_split; ++sp) {
+      const int64_t prow = (rec0 + sp) * 256 + rr;
+      const float2 ml = part_ml[prow];
+      if (!(ml.y > 0.f)) continue;
+      const float w = fast_exp2(ml.x - M);
+      const float2 o = *reinterpret_cast<const float2*>(part_o + prow * D + 2 * lane);
+      L = fmaf(ml.y, w, L);
+      ox = fmaf(o.x, w, ox);
+      oy = fmaf(o.y, w, oy);
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* dst = out + (int64_t(q_begin) + tok) * int64_t(H) * D + int64_t(g * group + hq) * D;
+    *reinterpret_cast<uint32_t*>(dst + 2 * lane) = pack2<T>(ox * inv, oy * inv);
+  }
+}
+
 template <typename T>
 CUtensorMapDataType tmap_dtype() {
   return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -493,7 +585,8 @@ template <typename T>
 int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
                 const void* v_cache, const int32_t* bt, int64_t bt_stride, const int32_t* cu,
                 const int32_t* lk, int R, int max_seqlen_q, int total_q, int H, int Kh,
-                int num_blocks, int max_blocks, float scale, cudaStream_t stream) {
+                int num_blocks, int max_blocks, float scale, int n_split, void* workspace,
+                cudaStream_t stream) {
   using Cfg = PairCfg;
   constexpr int D = Cfg::D;
   const int group = H / Kh;
@@ -529,28 +622,73 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
   }
   auto kern = prefill_pair_kernel<T>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  const int npairs = (max_seqlen_q + 2 * tq - 1) / (2 * tq);
-  dim3 grid(npairs, Kh, R);
+  const int npairs = pair_count(max_seqlen_q, H, Kh);
+  float2* part_ml = nullptr;
+  float* part_o = nullptr;
+  if (n_split > 1) {
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    const size_t rows = size_t(npairs) * Kh * R * n_split * 256;
+    part_ml = reinterpret_cast<float2*>(w);
+    part_o = reinterpret_cast<float*>(w + align256(rows * sizeof(float2)));
+  }
+  dim3 grid(npairs * n_split, Kh, R);
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
       mq, mk, mv, mk8, mv8, static_cast<T*>(out), bt, bt_stride, cu, lk, H, group, num_blocks,
-      max_blocks, scale * kLog2e, num_blocks >= 8 ? 1 : 0, device_status_ptr());
-  return check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
+      max_blocks, scale * kLog2e, num_blocks >= 8 ? 1 : 0, n_split, part_o, part_ml,
+      device_status_ptr());
+  int rc = check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
+  if (rc || n_split == 1) return rc;
+  prefill_merge_kernel<T><<<dim3(npairs, Kh, R), 256, 0, stream>>>(
+      static_cast<T*>(out), part_o, part_ml, cu, lk, H, H / Kh, npairs, n_split, max_blocks);
+  return check_launch("as_varlen_prefill_attention (split-KV merge)");
 }
 
 }  // namespace
+
+int prefill_pair_splits(int R, int max_seqlen_q, int H, int Kh, int max_blocks, int requested) {
+  if (requested > 0) return requested > kMaxSplits ? kMaxSplits : requested;
+  // Split the KV range of each query-tile pair when too few CTAs (one per SM) would
+  // otherwise run, e.g. a long cached prefix with a short new suffix.  Cost model:
+  // waves * (KV tiles per CTA + a fixed per-CTA cost measured at ~14.5 tile times
+  // on B200 (prologue, pipeline fill, epilogue, partial write and merge)); a split is
+  // taken only when it is predicted 25% faster.
+  constexpr double kCtaOverheadTiles = 14.5;
+  const int units = pair_count(max_seqlen_q, H, Kh) * Kh * R;
+  const int tiles = (max_blocks * kBS + PairCfg::kBN - 1) / PairCfg::kBN;
+  const int slots = sm_count();
+  int best = 1;
+  double best_cost = 0.0;
+  for (int sp = 1; sp <= kMaxSplits; ++sp) {
+    if (sp > 1 && tiles < 4 * sp) break;
+    const double waves = double((int64_t(units) * sp + slots - 1) / slots);
+    const double cost = waves * (double(tiles) / sp + kCtaOverheadTiles);
+    if (sp == 1 || cost < 0.75 * best_cost) {
+      best = sp;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+size_t prefill_pair_workspace_size(int R, int max_seqlen_q, int H, int Kh, int n_split) {
+  if (n_split <= 1) return 0;
+  const size_t rows = size_t(pair_count(max_seqlen_q, H, Kh)) * Kh * R * n_split * 256;
+  return align256(rows * sizeof(float2)) + align256(rows * PairCfg::D * sizeof(float));
+}
 
 int prefill_pair_launch(void* out, const void* q, int64_t q_stride, const void* k_cache,
                         const void* v_cache, const int32_t* bt, int64_t bt_stride,
                         const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int R,
                         int max_seqlen_q, int total_q, int H, int Kh, int num_blocks,
-                        int max_blocks, float scale, int dtype, cudaStream_t stream) {
+                        int max_blocks, float scale, int dtype, int n_split, void* workspace,
+                        cudaStream_t stream) {
   if (dtype == AS_DTYPE_BF16)
     return launch_pair<__nv_bfloat16>(out, q, q_stride, k_cache, v_cache, bt, bt_stride,
                                       cu_seqlens_q, seq_lens_k, R, max_seqlen_q, total_q, H, Kh,
-                                      num_blocks, max_blocks, scale, stream);
+                                      num_blocks, max_blocks, scale, n_split, workspace, stream);
   return launch_pair<__half>(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
                              seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks, max_blocks,
-                             scale, stream);
+                             scale, n_split, workspace, stream);
 }
 
 }  // namespace asb

@@ -538,7 +538,8 @@ int prefill_tc_launch(void* out, const void* q, int64_t q_stride, const void* k_
                       const void* v_cache, const int32_t* bt, int64_t bt_stride,
                       const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int R,
                       int max_seqlen_q, int total_q, int H, int Kh, int D, int num_blocks,
-                      int max_blocks, float scale, int dtype, cudaStream_t stream) {
+                      int max_blocks, float scale, int dtype, int n_split, void* workspace,
+                      cudaStream_t stream) {
   if (max_seqlen_q <= 0) return AS_OK;
   if (R > 65535) return fail(AS_ERR_INVALID_ARG, "as_varlen_prefill_attention: too many sequences");
 #ifndef AS_PREFILL_PAIR
@@ -547,7 +548,7 @@ int prefill_tc_launch(void* out, const void* q, int64_t q_stride, const void* k_
   if (AS_PREFILL_PAIR && D == 64)
     return prefill_pair_launch(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
                                seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks,
-                               max_blocks, scale, dtype, stream);
+                               max_blocks, scale, dtype, n_split, workspace, stream);
   if (dtype == AS_DTYPE_BF16) {
     using T = __nv_bfloat16;
     if (D == 64)

@@ -156,6 +156,10 @@ class B200LlamaModel(nn.Module):
         # forward_decode_paged replays a CUDA graph per (allocator, batch size, block
         # bucket) instead of launching ~5 kernels per layer from Python every step
         self.decode_graphs: bool = True
+        # projections of at most 256 tokens (the decode step) on the small-batch
+        # tensor-core kernel (as_linear_small_m) instead of cuBLAS
+        self.small_batch_linear: bool = True
+        self._lin_ws: Optional[torch.Tensor] = None
         self.max_decode_graphs: int = 16
         self._graphs: "OrderedDict[tuple, _PagedStepGraph]" = OrderedDict()
         self._graph_pool = None
@@ -191,12 +195,23 @@ class B200LlamaModel(nn.Module):
             f._gu_w = gu
         self._fused = True
 
+    def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        if (self.small_batch_linear and x.shape[0] <= ops.LINEAR_MAX_M and x.is_cuda
+                and x.dtype in (torch.bfloat16, torch.float16)):
+            if self._lin_ws is None:  # fixed size: CUDA graphs keep its address
+                c = self.config
+                max_n = max(self.H * self.D + 2 * self.Kh * self.D, c.hidden_dim,
+                            2 * c.intermediate_size)
+                self._lin_ws = ops.new_linear_workspace(ops.LINEAR_MAX_M, max_n, x.device)
+            return ops.linear_small_m(x, w, workspace=self._lin_ws)
+        return F.linear(x, w)
+
     def _qkv(self, layer: _Layer, h: torch.Tensor):
         n = h.shape[0]
         H, Kh, D = self.H, self.Kh, self.D
         a = layer.attn
         if self.fused_projections:
-            qkv = F.linear(h, a._qkv_w)
+            qkv = self._linear(h, a._qkv_w)
             return (qkv[:, :H * D].view(n, H, D), qkv[:, H * D:(H + Kh) * D].view(n, Kh, D),
                     qkv[:, (H + Kh) * D:].view(n, Kh, D))
         return (a.q_proj(h).view(n, H, D), a.k_proj(h).view(n, Kh, D), a.v_proj(h).view(n, Kh, D))
@@ -205,7 +220,7 @@ class B200LlamaModel(nn.Module):
         """SwiGLU on the already-normalised h (llama.py:207-211)."""
         f = layer.ffn
         if self.fused_projections:
-            return f.down_proj(ops.silu_mul(F.linear(h, f._gu_w)))
+            return self._linear(ops.silu_mul(self._linear(h, f._gu_w)), f.down_proj.weight)
         return f.down_proj(F.silu(f.gate_proj(h)) * f.up_proj(h))
 
     def _run_layers(self, x: torch.Tensor, attention) -> torch.Tensor:
@@ -216,7 +231,7 @@ class B200LlamaModel(nn.Module):
         L = len(self.layers)
         h = ops.rmsnorm(x, self.layers[0].attn_norm.weight, self.layers[0].attn_norm.eps)
         for li, layer in enumerate(self.layers):
-            a = layer.attn.o_proj(attention(li, layer, h))
+            a = self._linear(attention(li, layer, h), layer.attn.o_proj.weight)
             if self.tp_size > 1:  # row-parallel o_proj: sum the ranks' partial outputs
                 torch.distributed.all_reduce(a, group=self.tp_group)
             h = ops.add_rmsnorm(x, a, layer.ffn_norm.weight, layer.ffn_norm.eps)

@@ -232,25 +232,77 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
 # ---------------------------------------------------------------------------
 # (4) varlen prefill attention
 # ---------------------------------------------------------------------------
+def prefill_workspace_bytes(num_seqs: int, max_seqlen_q: int, num_heads: int, num_kv_heads: int,
+                            head_dim: int, max_blocks: int, num_splits: int = 0,
+                            dtype: torch.dtype = torch.bfloat16) -> int:
+    """Split-KV workspace of varlen_prefill_attention (0 when no split applies)."""
+    return int(N.load().as_varlen_prefill_workspace_size(
+        num_seqs, max_seqlen_q, num_heads, num_kv_heads, head_dim, max_blocks, num_splits,
+        dtype_code(dtype)))
+
+
 def varlen_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                              block_tables: torch.Tensor, cu_seqlens_q: torch.Tensor,
                              seq_lens_k: torch.Tensor, max_seqlen_q: int, scale: float,
-                             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                             out: Optional[torch.Tensor] = None, num_splits: int = 0,
+                             workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """q [total_q, H, D] (row-strided view allowed); returns out [total_q, H*D]
-    (head-major, as prefill flattens it: llama.py:184)."""
-    _cuda(q, k_cache, v_cache, block_tables, cu_seqlens_q, seq_lens_k, out)
+    (head-major, as prefill flattens it: llama.py:184).  num_splits: split-KV over
+    CTAs (0 = chosen by the library, 1 = off); its fp32 partials go to `workspace`
+    (uint8, prefill_workspace_bytes() long), allocated per call when not given."""
+    _cuda(q, k_cache, v_cache, block_tables, cu_seqlens_q, seq_lens_k, out, workspace)
     Tq, H, D = q.shape
     NB, bs, Kh, D2 = k_cache.shape
     assert bs == BLOCK_SIZE and D2 == D and _row_view_ok(q)
     assert block_tables.dtype == torch.int32 and block_tables.stride(1) == 1
     R = seq_lens_k.shape[0]
+    mb = block_tables.shape[1]
     if out is None:
         out = torch.empty(Tq, H * D, dtype=q.dtype, device=q.device)
-    N.check(N.load().as_varlen_prefill_attention(
+    if workspace is None and num_splits != 1:
+        need = prefill_workspace_bytes(R, int(max_seqlen_q), H, Kh, D, mb, num_splits, q.dtype)
+        if need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = _ptr(workspace) if workspace is not None else None
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    N.check(N.load().as_varlen_prefill_attention_ws(
         _ptr(out), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache), _ptr(block_tables),
         block_tables.stride(0), _ptr(cu_seqlens_q), _ptr(seq_lens_k), R, int(max_seqlen_q), Tq,
-        H, Kh, D, BLOCK_SIZE, NB, block_tables.shape[1], float(scale), dtype_code(q.dtype),
-        _stream(q.device)), "as_varlen_prefill_attention")
+        H, Kh, D, BLOCK_SIZE, NB, mb, float(scale), dtype_code(q.dtype), int(num_splits),
+        ws_ptr, ws_bytes, _stream(q.device)), "as_varlen_prefill_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (6) decode-step projections at small batch
+# ---------------------------------------------------------------------------
+LINEAR_MAX_M = 256
+
+
+def linear_workspace_bytes(max_m: int, max_n: int) -> int:
+    return int(N.load().as_linear_small_m_workspace_size(max_m, max_n))
+
+
+def new_linear_workspace(max_m: int, max_n: int, device) -> torch.Tensor:
+    """Zero-filled; the library leaves it zero after every call."""
+    return torch.zeros(linear_workspace_bytes(max_m, max_n), dtype=torch.uint8, device=device)
+
+
+def linear_small_m(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                   workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [M, K] (row-strided view allowed, M <= 256) @ w[N, K]^T -> [M, N]: nn.Linear
+    without bias on the tensor cores, K split over CTAs through `workspace`."""
+    _cuda(x, w, out, workspace)
+    M, K = x.shape
+    Nn = w.shape[0]
+    assert w.shape[1] == K and w.is_contiguous() and x.stride(1) == 1 and x.dtype == w.dtype
+    if out is None:
+        out = torch.empty(M, Nn, dtype=x.dtype, device=x.device)
+    assert out.stride(1) == 1
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    N.check(N.load().as_linear_small_m(
+        _ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, Nn, K, dtype_code(x.dtype),
+        _ptr(workspace), ws_bytes, _stream(x.device)), "as_linear_small_m")
     return out
 
 

@@ -255,13 +255,17 @@ def measure_prefill(dev, reps: int = 10):
                           dtype=torch.int32, device=dev)
         lk = torch.tensor(lens, dtype=torch.int32, device=dev)
         out = torch.empty(sum(num_new), H * D, device=dev, dtype=torch.bfloat16)
+        need = ops.prefill_workspace_bytes(R, max(num_new), H, Kh, D, bt.shape[1])
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
         for _ in range(2):
-            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out)
+            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out,
+                                         workspace=ws)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out)
+            ops.varlen_prefill_attention(q, kp, vp, bt, cu, lk, max(num_new), D ** -0.5, out=out,
+                                         workspace=ws)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps

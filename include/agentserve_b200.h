@@ -203,6 +203,53 @@ AS_API int as_varlen_prefill_attention(void* out, const void* q, int64_t q_strid
                                 int32_t num_blocks, int32_t max_blocks, float scale,
                                 int32_t dtype, as_stream_t stream);
 
+/* Same computation with split-KV (same reference interface, llama.py:128-186): for
+ * head_dim 64 in bf16/f16 the key range of every query tile pair can be divided over
+ * num_splits CTAs, whose partial results (fp32) go to `workspace` and are combined by
+ * a second kernel on the same stream.  This fills the GPU when few sequences are
+ * prefilled at once (the reference prefills one request per call, engine.py:228-229).
+ * num_splits: 0 = chosen from the grid shape and SM count, 1 = no split, k > 1 = k
+ * (at most 16).  workspace: as_varlen_prefill_workspace_size() bytes, 256-byte aligned;
+ * it needs no initialisation.  With num_splits = 0 and too small (or NULL) a workspace
+ * the call runs unsplit; with k > 1 it fails with AS_ERR_WORKSPACE.  Shapes the split
+ * does not apply to ignore num_splits and workspace. */
+AS_API int as_varlen_prefill_attention_ws(void* out, const void* q, int64_t q_stride,
+                                          const void* k_cache, const void* v_cache,
+                                          const int32_t* block_tables, int64_t bt_stride,
+                                          const int32_t* cu_seqlens_q,
+                                          const int32_t* seq_lens_k, int32_t num_seqs,
+                                          int32_t max_seqlen_q, int32_t total_q,
+                                          int32_t num_heads, int32_t num_kv_heads,
+                                          int32_t head_dim, int32_t block_size,
+                                          int32_t num_blocks, int32_t max_blocks, float scale,
+                                          int32_t dtype, int32_t num_splits, void* workspace,
+                                          size_t workspace_bytes, as_stream_t stream);
+
+/* Workspace bytes as_varlen_prefill_attention_ws needs for these sizes and num_splits
+ * (0 when no split applies). */
+AS_API size_t as_varlen_prefill_workspace_size(int32_t num_seqs, int32_t max_seqlen_q,
+                                               int32_t num_heads, int32_t num_kv_heads,
+                                               int32_t head_dim, int32_t max_blocks,
+                                               int32_t num_splits, int32_t dtype);
+
+/* ------------------------------------------------------------------------- */
+/* (6) Decode-step projections at small batch                                */
+/* ------------------------------------------------------------------------- */
+
+/* y[m, n] = sum_k x[m, k] * w[n, k] for m < M <= 256 (nn.Linear without bias: the
+ * q/k/v, o_proj, gate/up and down projections of the decode step, llama.py:123-126,
+ * 203-211, 430-431, 471), bf16/fp16, fp32 accumulation.  Row strides y_stride and
+ * x_stride in elements; w is [N, K] row-major (nn.Linear.weight).  The K range is split
+ * over CTAs when N/128 alone cannot fill the GPU; the partial sums then go through
+ * `workspace` (as_linear_small_m_workspace_size(M, N) bytes, 256-byte aligned, zero
+ * on first use; the library leaves it zero after every call — after a call that set
+ * a device status bit, zero it again).  A NULL or smaller workspace disables the
+ * split.  Calls sharing a workspace must be ordered on one stream. */
+AS_API size_t as_linear_small_m_workspace_size(int32_t M, int32_t N);
+AS_API int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64_t x_stride,
+                             const void* w, int32_t M, int32_t N, int32_t K, int32_t dtype,
+                             void* workspace, size_t workspace_bytes, as_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* (5) Block gather / copy (prefix-cache seeding, gather_kv)                 */
 /* ------------------------------------------------------------------------- */

@@ -31,7 +31,8 @@ def test_header_declares_entry_points():
     syms = declared_symbols()
     for name in ("as_pack_decode", "as_pack_prefill", "as_rope_reshape_and_cache",
                  "as_paged_decode_attention", "as_varlen_prefill_attention", "as_block_copy",
-                 "as_paged_decode_workspace_size", "as_last_error", "as_device_status"):
+                 "as_paged_decode_workspace_size", "as_last_error", "as_device_status",
+                 "as_varlen_prefill_attention_ws", "as_varlen_prefill_workspace_size"):
         assert name in syms
 
 

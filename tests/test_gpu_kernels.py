@@ -352,6 +352,92 @@ def test_prefill_consecutive_block_runs(D):
     status_ok()
 
 
+@pytest.mark.parametrize("num_splits", [2, 3, 5, 8, 16])
+def test_prefill_split_kv_vs_oracle(num_splits):
+    """Split-KV prefill (head_dim 64): each query-tile pair's key range divided over
+    CTAs and merged; sequences shorter than the split count (empty splits), prefixes
+    that end mid-tile and causal tails inside the last splits."""
+    num_cached = [3000, 0, 37, 700, 16, 1]
+    num_new = [90, 5, 64, 200, 1, 129]
+    tables, kp, vp, q, cu, lens = prefill_case(num_cached, num_new, 32, 8, 64, torch.bfloat16,
+                                               seed=90 + num_splits)
+    bt = padded(tables).to(DEV)
+    need = ops.prefill_workspace_bytes(len(lens), max(num_new), 32, 8, 64, bt.shape[1],
+                                       num_splits)
+    assert need > 0
+    ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+    out = ops.varlen_prefill_attention(q.to(DEV), kp.to(DEV), vp.to(DEV), bt,
+                                       torch.from_numpy(cu).to(DEV),
+                                       torch.tensor(lens, dtype=torch.int32, device=DEV),
+                                       max(num_new), 0.125, num_splits=num_splits,
+                                       workspace=ws).cpu()
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+def test_prefill_split_kv_auto_one_request_and_workspace_rules():
+    """One request with a long cached prefix and a short suffix (8 CTAs unsplit) takes
+    an automatic split; forcing a split without enough workspace is an error, while
+    the automatic choice falls back to no split."""
+    tables, kp, vp, q, cu, lens = prefill_case([30000], [16], 32, 8, 64, torch.bfloat16, 78)
+    bt = padded(tables).to(DEV)
+    args = (q.to(DEV), kp.to(DEV), vp.to(DEV), bt, torch.from_numpy(cu).to(DEV),
+            torch.tensor(lens, dtype=torch.int32, device=DEV), 16, 0.125)
+    assert ops.prefill_workspace_bytes(1, 16, 32, 8, 64, bt.shape[1]) > 0  # auto splits here
+    auto = ops.varlen_prefill_attention(*args).cpu()
+    ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
+    torch.testing.assert_close(auto.float(), ref, rtol=0, atol=ATOL_LOWP)
+    small = torch.empty(256, dtype=torch.uint8, device=DEV)
+    with pytest.raises(ValueError):
+        ops.varlen_prefill_attention(*args, num_splits=4, workspace=small)
+    fallback = ops.varlen_prefill_attention(*args, num_splits=0, workspace=small).cpu()
+    unsplit = ops.varlen_prefill_attention(*args, num_splits=1).cpu()
+    assert torch.equal(fallback, unsplit)
+    torch.testing.assert_close(unsplit.float(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
+
+
+# ---------------------------------------------------------------- small-batch projections
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(64, 3072, 2048), (1, 2048, 2048), (7, 16384, 2048),
+                                   (64, 2048, 8192), (100, 130, 72), (128, 4096, 4096),
+                                   (200, 6144, 4096), (256, 512, 1024)])
+def test_linear_small_m_vs_fp32(dtype, M, N, K):
+    """as_linear_small_m against an fp32 matmul of the same (rounded) inputs: N not a
+    multiple of the 128-row tile, K not a multiple of the 64-wide stage, M from 1 to
+    256; split-K through the workspace, which is zero again after every call."""
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    x = (torch.randn(M, K, generator=g) * 0.5).to(dtype).to(DEV)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(dtype).to(DEV)
+    ws = ops.new_linear_workspace(M, N, DEV)
+    y = ops.linear_small_m(x, w, workspace=ws)
+    ref = x.float() @ w.float().t()
+    tol = 2e-2 * max(1.0, float(ref.abs().max()))
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=tol)
+    assert int(ws.count_nonzero()) == 0
+    y2 = ops.linear_small_m(x, w, workspace=ws)  # second call on the same workspace
+    torch.testing.assert_close(y2.float(), y.float(), rtol=1e-2, atol=tol)  # fp32 atomics: order varies
+    y1 = ops.linear_small_m(x, w)                # no workspace: one CTA per N tile
+    torch.testing.assert_close(y1.float(), ref, rtol=1e-2, atol=tol)
+    status_ok()
+
+
+def test_linear_small_m_strided_x_and_out():
+    """x as a column slice of a wider buffer and y written into a slice of another."""
+    g = torch.Generator().manual_seed(3)
+    buf = torch.randn(48, 3072, generator=g).to(torch.bfloat16).to(DEV)
+    x = buf[:, 1024:3072]
+    w = (torch.randn(2560, 2048, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    out = torch.zeros(48, 4096, dtype=torch.bfloat16, device=DEV)
+    ws = ops.new_linear_workspace(48, 2560, DEV)
+    ops.linear_small_m(x, w, out=out[:, 512:3072], workspace=ws)
+    ref = x.float() @ w.float().t()
+    torch.testing.assert_close(out[:, 512:3072].float(), ref, rtol=1e-2, atol=2e-2)
+    assert int(out[:, :512].count_nonzero()) == 0 and int(out[:, 3072:].count_nonzero()) == 0
+    status_ok()
+
+
 # ---------------------------------------------------------------- block copy
 def test_block_copy_gather_and_seed_bit_exact():
     g = torch.Generator().manual_seed(6)

@@ -293,3 +293,56 @@ def test_forward_decode_paged_graphs_match_eager(bps):
         else:
             torch.testing.assert_close(gr, e, rtol=0, atol=2e-2)
     m.release_decode_graphs()
+
+
+def test_zero_copy_prefix_sharing_prefill_and_decode():
+    """A finished request's full prefix blocks are retained and shared by two later
+    requests (no K/V copy); their prefill over the shared blocks and the following
+    decode steps match the oracle, and the shared blocks are never written."""
+    cfg = ModelConfig(**PAGED_CFG)
+    m = b200_model(cfg, torch.float32, fused=True)
+    o = OracleLlama(cfg).to(DEV)
+    init_weights_(o, seed=0)
+    o.eval()
+    g = torch.Generator().manual_seed(12)
+    shared = torch.randint(3, cfg.vocab_size, (160,), generator=g).tolist()  # 10 full blocks
+    a = DeviceBlockAllocator(128, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                             dtype=torch.float32, device=DEV)
+    a.allocate("first", a.blocks_needed(len(shared) + 7))
+    m.forward_prefill_paged([shared + [5, 6, 7]], [0], a, ["first"])
+    prefix = a.blocks_for("first")[:10]
+    a.retain_blocks(prefix)
+    a.free("first")
+    snap = a.kv_pool[:, :, prefix].clone()
+    suffixes = [torch.randint(3, cfg.vocab_size, (n,), generator=g).tolist() for n in (37, 5)]
+    prompts = [shared + sfx for sfx in suffixes]
+    rids = ["s0", "s1"]
+    for r, p in zip(rids, prompts):
+        a.share_blocks(r, prefix)
+        a.allocate(r, a.blocks_needed(len(p) + 4) - len(prefix))
+    logits = m.forward_prefill_paged(prompts, [160, 160], a, rids)
+    oa = OracleBlockAllocator(128, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                              allocate_tensor=True, device=DEV)
+    last, pos = [], []
+    for i, (r, p) in enumerate(zip(rids, prompts)):
+        lo, kvo = _oracle_prefill(o, p, 160)
+        torch.testing.assert_close(logits[i], lo, rtol=0, atol=2e-4)
+        oa.allocate(r, oa.blocks_needed(len(p) + 4))
+        for li in range(cfg.n_layers):
+            oa.write_kv_prefill(r, li, *kvo[li])
+        last.append(int(lo.argmax()))
+        pos.append(len(p))
+    assert greedy(logits).tolist() == last
+    lm_last = list(last)
+    for _ in range(3):
+        lm, _ = m.forward_decode_paged(lm_last, pos, pos, a, rids)
+        lo, _ = o.forward_decode_paged(last, pos, pos, oa, rids)
+        torch.testing.assert_close(lm, lo, rtol=0, atol=2e-4)
+        lm_last, last = greedy(lm).tolist(), greedy(lo).tolist()
+        assert lm_last == last
+        pos = [x + 1 for x in pos]
+    assert torch.equal(a.kv_pool[:, :, prefix], snap)  # shared blocks never written
+    for r in rids:
+        a.free(r)
+    a.release_blocks(prefix)
+    assert a.num_used_blocks() == 0

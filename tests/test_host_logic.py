@@ -114,3 +114,31 @@ def test_decode_workspace_zeroes_counters_only_when_they_grow():
     b2[64 * 32 * 4:].fill_(3)
     b3 = ws.get(8, 64, 16)  # smaller counter region: already zero, no memset needed
     assert int(b3[:8 * 32 * 4].sum()) == 0
+
+
+def test_zero_copy_prefix_sharing_ref_counts(alloc):
+    """A prefix-cache entry retains a finished request's full prefix blocks; a later
+    request shares them (ref counts, no copy) and allocates the rest; blocks go back to
+    the free list only when the last holder lets go."""
+    a = alloc.allocate("A", 5)
+    prefix = a[:3]
+    alloc.retain_blocks(prefix)           # cache entry
+    alloc.free("A")
+    assert alloc.num_used_blocks() == 3 and all(alloc.ref_count(b) == 1 for b in prefix)
+    alloc.share_blocks("B", prefix)
+    own = alloc.allocate("B", 2)
+    assert alloc.blocks_for("B") == prefix + own
+    assert alloc.block_tables[alloc.row_of("B"), :5].tolist() == prefix + own
+    assert all(alloc.ref_count(b) == 2 for b in prefix)
+    alloc.share_blocks("C", prefix[:2])
+    alloc.free("B")
+    assert all(alloc.ref_count(b) == (2 if b in prefix[:2] else 1) for b in prefix)
+    alloc.release_blocks(prefix)          # cache entry evicted
+    assert alloc.ref_count(prefix[2]) == 0 and prefix[2] in alloc._free
+    alloc.free("C")
+    assert alloc.num_used_blocks() == 0 and alloc.num_free_blocks() == 32
+    with pytest.raises(ValueError):
+        alloc.share_blocks("D", [prefix[0]])  # no longer allocated
+    alloc.allocate("E", 1)
+    with pytest.raises(ValueError):
+        alloc.share_blocks("E", alloc.blocks_for("E"))  # must share before allocating
