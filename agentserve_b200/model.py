@@ -156,9 +156,11 @@ class B200LlamaModel(nn.Module):
         # forward_decode_paged replays a CUDA graph per (allocator, batch size, block
         # bucket) instead of launching ~5 kernels per layer from Python every step
         self.decode_graphs: bool = True
-        # projections of at most 256 tokens (the decode step) on the small-batch
-        # tensor-core kernel (as_linear_small_m) instead of cuBLAS
-        self.small_batch_linear: bool = True
+        # True: projections of at most 256 tokens (the decode step) on the small-batch
+        # tensor-core kernel (as_linear_small_m) instead of cuBLAS.  Off by default:
+        # measured slower than cuBLAS on B200 at batch 64 (split-K global reductions
+        # and per-CTA TMA weight streaming are the limits).
+        self.small_batch_linear: bool = False
         self._lin_ws: Optional[torch.Tensor] = None
         self.max_decode_graphs: int = 16
         self._graphs: "OrderedDict[tuple, _PagedStepGraph]" = OrderedDict()

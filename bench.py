@@ -466,10 +466,12 @@ def run_b200(args):
                          "traffic_source": (traffic or {}).get("source")},
             "e2e": {"value": e2e_value, "unit": "tok/s", "api": "B200LlamaModel.forward_decode_paged"
                     "(host lists) + greedy + .cpu()",
-                    "h2d_bytes_per_step": 4 * B * 8, "d2h_bytes_per_step": B * 8},
-            # per step: pack + first RMSNorm + per layer (RoPE/cache, attention,
-            # 2 x add+RMSNorm, SwiGLU)
-            "gpu_launches": args.steps * (2 + 5 * cfg.n_layers),
+                    # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
+                    # the greedy int64 tokens out
+                    "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8},
+            # per step: pack + first RMSNorm + per layer (QKV, o_proj, gate/up and down
+            # projections, RoPE/cache, attention, 2 x add+RMSNorm, SwiGLU)
+            "gpu_launches": args.steps * (2 + 9 * cfg.n_layers),
             "prefill": None if pf is None else {
                 "kernel": "varlen prefill attention, tcgen05 + TMEM (bf16, D=64, GQA 4)",
                 "shape": "prefix 14336 + 600 new tokens per request (prefix-cache workload)",

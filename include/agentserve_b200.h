@@ -23,6 +23,9 @@
  *   as_paged_decode_attention llama.py:419-469 (gather_kv -> pad -> GQA expand -> SDPA)
  *                             and llama.py:303-361 (padded-list decode)
  *   as_varlen_prefill_attention llama.py:128-186 (prefill over cached prefix + new tokens)
+ *   as_varlen_prefill_attention_ws  the same, split-KV over CTAs with a workspace
+ *   as_linear_small_m         nn.Linear of the decode step (llama.py:123-126, 203-211,
+ *                             430-431, 471): q/k/v, o_proj, gate/up, down at batch <= 256
  *   as_block_copy             cache.py:158-189 (gather_kv) and engine.py:274-281,338-345
  *                             (prefix-cache KV clone / seed)
  *   as_rmsnorm / as_add_rmsnorm / as_silu_mul
