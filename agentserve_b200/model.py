@@ -9,9 +9,10 @@ methods Engine uses:
   forward_decode_paged(last, seq_lens, pos, allocator, request_ids)
                                                         llama.py:379-475, engine.py:360-366
 
-Attention, RoPE, KV writes, packing and block gathers are the library's kernels;
-norms, projections (cuBLAS through torch), SwiGLU, lm_head and greedy argmax stay
-torch ops, as in the reference.  With reference_compat=True (default) two
+Attention, RoPE, KV writes, packing, block gathers, RMSNorm (+ residual add),
+SwiGLU and greedy argmax are the library's kernels; the projections and lm_head are
+cuBLAS GEMMs through torch (the library's small-batch projection kernel is optional,
+`small_batch_linear`).  With reference_compat=True (default) two
 behaviours of the reference's decode paths are reproduced so results match it:
 the decode attention output is flattened dim-major before o_proj (llama.py:362,
 470), and forward_decode_batch returns, for every sequence shorter than the
@@ -535,9 +536,9 @@ class _PagedStepGraph:
 
 
 def greedy(logits: torch.Tensor) -> torch.Tensor:
-    """sampling.py:46-58 with temperature <= 1e-6: fp32, nan_to_num, argmax."""
-    lf = torch.nan_to_num(logits.float(), nan=0.0, posinf=1e4, neginf=-1e4)
-    return lf.argmax(dim=-1)
+    """sampling.py:46-58 with temperature <= 1e-6 (fp32, nan_to_num(0, 1e4, -1e4),
+    first argmax) for [B, V] logits, in one kernel (as_greedy_argmax)."""
+    return ops.greedy_argmax(logits)
 
 
 class DecodeGraph:

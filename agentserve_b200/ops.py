@@ -307,6 +307,37 @@ def linear_small_m(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]
 
 
 # ---------------------------------------------------------------------------
+# (7) greedy sampling
+# ---------------------------------------------------------------------------
+GREEDY_WS_ROWS = 4096
+_greedy_ws: dict = {}
+
+
+def greedy_argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[B, V] logits -> [B] int64 token ids: the reference's greedy sampling (fp32,
+    nan_to_num(0, 1e4, -1e4), first argmax) in one kernel.  Its small workspace is one
+    fixed buffer per device (so CUDA graphs keep its address), for up to 4096 rows."""
+    _cuda(logits, out)
+    B, V = logits.shape
+    assert logits.stride(1) == 1
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=logits.device)
+    if B > GREEDY_WS_ROWS:
+        ws = torch.zeros(int(N.load().as_greedy_workspace_size(B)), dtype=torch.uint8,
+                         device=logits.device)
+    else:
+        ws = _greedy_ws.get(logits.device)
+        if ws is None:
+            ws = _greedy_ws[logits.device] = torch.zeros(
+                int(N.load().as_greedy_workspace_size(GREEDY_WS_ROWS)), dtype=torch.uint8,
+                device=logits.device)
+    N.check(N.load().as_greedy_argmax(
+        _ptr(out), _ptr(logits), logits.stride(0), B, V, dtype_code(logits.dtype), _ptr(ws),
+        ws.numel(), _stream(logits.device)), "as_greedy_argmax")
+    return out
+
+
+# ---------------------------------------------------------------------------
 # (5) block gather / copy
 # ---------------------------------------------------------------------------
 def block_copy(dst: torch.Tensor, src: torch.Tensor, src_ids: torch.Tensor,

@@ -469,9 +469,9 @@ def run_b200(args):
                     # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
                     # the greedy int64 tokens out
                     "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8},
-            # per step: pack + first RMSNorm + per layer (QKV, o_proj, gate/up and down
-            # projections, RoPE/cache, attention, 2 x add+RMSNorm, SwiGLU)
-            "gpu_launches": args.steps * (2 + 9 * cfg.n_layers),
+            # per step: pack + first RMSNorm + greedy argmax + per layer (RoPE/cache,
+            # attention, 2 x add+RMSNorm, SwiGLU); the projections and lm_head are cuBLAS
+            "gpu_launches": args.steps * (3 + 5 * cfg.n_layers),
             "prefill": None if pf is None else {
                 "kernel": "varlen prefill attention, tcgen05 + TMEM (bf16, D=64, GQA 4)",
                 "shape": "prefix 14336 + 600 new tokens per request (prefix-cache workload)",

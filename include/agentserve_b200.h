@@ -26,6 +26,7 @@
  *   as_varlen_prefill_attention_ws  the same, split-KV over CTAs with a workspace
  *   as_linear_small_m         nn.Linear of the decode step (llama.py:123-126, 203-211,
  *                             430-431, 471): q/k/v, o_proj, gate/up, down at batch <= 256
+ *   as_greedy_argmax          sampling.py:46-58 (greedy branch) + engine.py:379-383
  *   as_block_copy             cache.py:158-189 (gather_kv) and engine.py:274-281,338-345
  *                             (prefix-cache KV clone / seed)
  *   as_rmsnorm / as_add_rmsnorm / as_silu_mul
@@ -252,6 +253,21 @@ AS_API size_t as_linear_small_m_workspace_size(int32_t M, int32_t N);
 AS_API int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64_t x_stride,
                              const void* w, int32_t M, int32_t N, int32_t K, int32_t dtype,
                              void* workspace, size_t workspace_bytes, as_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* (7) Greedy sampling                                                        */
+/* ------------------------------------------------------------------------- */
+
+/* out[r] = index of the first maximum of row r of logits [num_rows, vocab] (row
+ * stride in elements) after the reference's sanitising (sampling.py:46-58 at
+ * temperature <= 1e-6: fp32, NaN -> 0, +inf -> 1e4, -inf -> -1e4), in one pass over
+ * the logits.  workspace: as_greedy_workspace_size(num_rows) bytes, 256-byte aligned,
+ * zero on first use; the library leaves it zero (calls sharing it must be ordered on
+ * one stream). */
+AS_API size_t as_greedy_workspace_size(int32_t num_rows);
+AS_API int as_greedy_argmax(int64_t* out, const void* logits, int64_t row_stride,
+                            int32_t num_rows, int32_t vocab, int32_t dtype, void* workspace,
+                            size_t workspace_bytes, as_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* (5) Block gather / copy (prefix-cache seeding, gather_kv)                 */

@@ -168,3 +168,10 @@ class OracleLlama(nn.Module):
             x = x + layer.attn.o_proj(flatten_decode_output(attn))
             x = x + layer.ffn(layer.ffn_norm(x))
         return self.lm_head(self.norm(x)), None
+
+
+def greedy(logits):
+    """sampling.py:46-58 at temperature <= 1e-6: fp32 upcast, NaN -> 0, +inf -> 1e4,
+    -inf -> -1e4, argmax (first maximum)."""
+    lf = torch.nan_to_num(logits.float(), nan=0.0, posinf=1e4, neginf=-1e4)
+    return lf.argmax(dim=-1)

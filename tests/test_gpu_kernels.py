@@ -438,6 +438,38 @@ def test_linear_small_m_strided_x_and_out():
     status_ok()
 
 
+# ---------------------------------------------------------------- greedy sampling
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("B,V", [(64, 128256), (3, 1000), (5, 4097), (2, 1), (130, 8192)])
+def test_greedy_argmax_matches_reference_sampling(dtype, B, V):
+    """as_greedy_argmax equals sampling.py's greedy branch (fp32, nan_to_num(0, 1e4,
+    -1e4), first argmax) index for index: NaN, +-inf, ties at two positions, -0/+0,
+    rows of -inf only, chunk boundaries."""
+    from oracle.model import greedy as oracle_greedy
+    g = torch.Generator().manual_seed(B * 31 + V)
+    x = torch.randn(B, V, generator=g) * 3
+    if V > 10:
+        x[0, 7] = float("nan")
+        x[0, V // 2] = float("inf")                # -> 1e4: the row maximum
+        x[1, :] = -float("inf")                     # all -1e4: first index
+        x[2, 3] = x[2, V - 2] = x[2].max() + 1.0    # tie: the first one wins
+        if B > 3:
+            x[3, :] = 0.0
+            x[3, 5] = -0.0                          # -0 and +0 tie: first index (0)
+        if B > 4:
+            x[4, 4096] = 50.0 if V > 4096 else x[4, 4096 % V]  # max in the second chunk
+            x[4, 4095] = 50.0 if V > 4096 else x[4, 4095 % V]  # equal max just before it
+    xd = x.to(dtype).to(DEV)
+    got = ops.greedy_argmax(xd).cpu()
+    want = oracle_greedy(xd).cpu()
+    assert torch.equal(got, want)
+    # twice in a row on the same (self-resetting) workspace, and on a row-strided view
+    wide = torch.zeros(B, V + 24, dtype=dtype, device=DEV)
+    wide[:, :V] = xd
+    assert torch.equal(ops.greedy_argmax(wide[:, :V]).cpu(), want)
+    status_ok()
+
+
 # ---------------------------------------------------------------- block copy
 def test_block_copy_gather_and_seed_bit_exact():
     g = torch.Generator().manual_seed(6)

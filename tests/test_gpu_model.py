@@ -14,6 +14,7 @@ import torch
 from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, greedy
 from agentserve_b200.config import ModelConfig
 from oracle.model import OracleLlama
+from oracle.model import greedy as oracle_greedy
 from oracle.paged import OracleBlockAllocator
 from oracle.rope import precompute_rope_freqs
 from oracle.weights import init_weights_
@@ -125,7 +126,7 @@ def test_greedy_256_steps_identical_fp32_llama1b():
         lm, _ = m.forward_decode_paged(last_m, lens, lens, a, rids)
         lo, _ = o.forward_decode_paged(last_o, lens, lens, oa, rids)
         last_m = greedy(lm).tolist()
-        last_o = greedy(lo).tolist()
+        last_o = oracle_greedy(lo).tolist()
         if last_m != last_o:
             top2 = torch.topk(lo.float(), 2, dim=-1).values
             margin = (top2[:, 0] - top2[:, 1]).min().item()
@@ -238,7 +239,7 @@ def test_batched_paged_prefill_with_seeded_prefixes(dtype):
             lm, _ = m.forward_decode_paged(lm_last, pos, pos, a, rids)
             lo, _ = o.forward_decode_paged(last, pos, pos, oa, rids)
             torch.testing.assert_close(lm, lo, rtol=0, atol=atol)
-            lm_last, last = greedy(lm).tolist(), greedy(lo).tolist()
+            lm_last, last = greedy(lm).tolist(), oracle_greedy(lo).tolist()
             assert lm_last == last
             pos = [x + 1 for x in pos]
 
