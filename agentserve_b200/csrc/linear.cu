@@ -38,7 +38,10 @@ namespace {
 
 constexpr int kTileN = kLinTileN;
 constexpr int kTileK = 64;
-constexpr int kStages = 4;
+#ifndef AS_LINEAR_STAGES
+#define AS_LINEAR_STAGES 4
+#endif
+constexpr int kStages = AS_LINEAR_STAGES;
 constexpr int kMaxM = 256;
 constexpr int kWBytes = kTileN * 128;  // 128 rows x 64 16-bit elements
 

@@ -53,6 +53,12 @@ int pair_count(int max_seqlen_q, int H, int Kh) {
 #ifndef AS_PREFILL_PINGPONG
 #define AS_PREFILL_PINGPONG 1
 #endif
+// The exponent-unit turn passes to the partner warp after this many of the 64 column
+// pairs (64: at the end), so the hand-off latency overlaps the remaining pairs
+// (measured on B200, 8 requests: 64 -> 566-571, 32 -> 604-606 TFLOP/s).
+#ifndef AS_PREFILL_HANDOFF
+#define AS_PREFILL_HANDOFF 32
+#endif
 // ---- packed fp32 pairs (sm_100 f32x2 arithmetic) --------------------------------
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
   uint64_t r;
@@ -431,6 +437,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         float p0, p1;
         f2_unpack(p2, p0, p1);
         pk[c] = pack2<T>(p0, p1);
+        if (AS_PREFILL_PINGPONG && AS_PREFILL_HANDOFF < 64 && c == AS_PREFILL_HANDOFF - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
+        }
       }
       float sum;
       {
@@ -439,7 +449,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         f2_unpack(s01, a, b);
         sum = a + b;
       }
-      if (AS_PREFILL_PINGPONG) {
+      if (AS_PREFILL_PINGPONG && AS_PREFILL_HANDOFF >= 64) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
       }
