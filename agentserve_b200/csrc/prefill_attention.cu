@@ -148,10 +148,11 @@ using namespace asb;
 
 namespace {
 
-// head_dim 64 on the tensor cores takes the query-tile-pair kernel, which can split KV
+// the tensor-core shapes take the query-tile-pair kernel, which can split KV
 bool pair_path(int32_t dtype, int32_t H, int32_t Kh, int32_t D, const void* q, int64_t q_stride,
                const void* k_cache, const void* v_cache, const void* out) {
-  return D == 64 && prefill_tc_supported(dtype, H, Kh, D, q, q_stride, k_cache, v_cache, out);
+  return (D == 64 || D == 128) &&
+         prefill_tc_supported(dtype, H, Kh, D, q, q_stride, k_cache, v_cache, out);
 }
 
 int prefill_entry(void* out, const void* q, int64_t q_stride, const void* k_cache,
@@ -184,7 +185,7 @@ int prefill_entry(void* out, const void* q, int64_t q_stride, const void* k_cach
       n_split = prefill_pair_splits(num_seqs, max_seqlen_q, num_heads, num_kv_heads, max_blocks,
                                     num_splits);
       const size_t need = prefill_pair_workspace_size(num_seqs, max_seqlen_q, num_heads,
-                                                      num_kv_heads, n_split);
+                                                      num_kv_heads, head_dim, n_split);
       if (need > 0 && (!workspace || workspace_bytes < need)) {
         if (num_splits > 1)
           return fail(AS_ERR_WORKSPACE, "as_varlen_prefill_attention: workspace of %zu bytes < %zu",
@@ -258,10 +259,11 @@ extern "C" size_t as_varlen_prefill_workspace_size(int32_t num_seqs, int32_t max
       num_heads % num_kv_heads || max_blocks <= 0 || num_splits == 1 || num_splits < 0)
     return 0;
   const int group = num_heads / num_kv_heads;
-  if (head_dim != 64 || (dtype != AS_DTYPE_BF16 && dtype != AS_DTYPE_F16) || group > 128 ||
-      128 % group)
+  if ((head_dim != 64 && head_dim != 128) || (dtype != AS_DTYPE_BF16 && dtype != AS_DTYPE_F16) ||
+      group > 128 || 128 % group)
     return 0;
   const int n = prefill_pair_splits(num_seqs, max_seqlen_q, num_heads, num_kv_heads, max_blocks,
                                     num_splits);
-  return prefill_pair_workspace_size(num_seqs, max_seqlen_q, num_heads, num_kv_heads, n);
+  return prefill_pair_workspace_size(num_seqs, max_seqlen_q, num_heads, num_kv_heads, head_dim,
+                                     n);
 }

@@ -1,5 +1,5 @@
-// (4) Varlen prefill attention, head_dim 64: two query tiles per CTA sharing every
-// K/V tile, P kept in tensor memory.
+// (4) Varlen prefill attention, head_dim 64 and 128: two query tiles per CTA sharing
+// every K/V tile, P kept in tensor memory.
 //
 // Semantics as in prefill_tcgen05.cu (LlamaAttention.forward over a cached prefix,
 // agentserve/model/llama.py:128-186): token i of a sequence with P cached tokens
@@ -23,7 +23,8 @@
 //               SM sub-partition take turns on its exponent unit (ping-pong), so one
 //               warp's TMEM loads, stores and waits overlap the other's exponentials.
 // TMEM (512 columns): tile i owns [256 i, 256 i + 256): S 128 columns, P 64 columns
-// (128 keys as 16-bit pairs), O 64 columns.  Every wait is bounded; a wait that
+// (128 keys as 16-bit pairs), O D columns (at D=128 P overlays S; see PairCfg).
+// Every wait is bounded; a wait that
 // runs out sets status bit 4, the CTA stops issuing, drains its MMAs, frees TMEM
 // and writes nothing.
 #include <type_traits>
@@ -84,18 +85,29 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+template <int HD>
 struct PairCfg {
-  static constexpr int D = 64;
+  static constexpr int D = HD;
   static constexpr int kBM = 128;
   static constexpr int kBN = 128;
-  static constexpr int kStages = AS_PREFILL_PAIR_STAGES;
-  static constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 B (64 16-bit elements)
-  static constexpr int kOffQ = 0;               // Q tile i at kOffQ + i * kTileBytes
-  static constexpr int kOffKV = 2 * kTileBytes;  // stage s: K at +2s*kTileBytes, V after it
-  static constexpr int kOffBar = kOffKV + kStages * 2 * kTileBytes;
+  static constexpr int kSub = D / 64;             // 64-element (128 B) swizzle sub-tiles
+  static constexpr int kSubBytes = 128 * 128;     // 128 rows x 128 B
+  static constexpr int kQBytes = kSub * kSubBytes;   // one query tile
+  static constexpr int kKVBytes = kSub * kSubBytes;  // K (or V) of one KV tile
+  static constexpr int kStages = D == 64 ? AS_PREFILL_PAIR_STAGES : 2;
+  static constexpr int kOffQ = 0;                    // Q tile i at kOffQ + i * kQBytes
+  static constexpr int kOffKV = 2 * kQBytes;         // stage s: K at +2s*kKVBytes, V after it
+  static constexpr int kOffBar = kOffKV + kStages * 2 * kKVBytes;
   static constexpr int kSmemBytes = kOffBar + 512;
   static constexpr int kThreads = 320;
   static constexpr int kTmemCols = 512;
+  // TMEM columns of query tile i, from 256 i: S [0, 128); at D=64 P [128, 192) and
+  // O [192, 256); at D=128 O [128, 256) and P aliased onto S [0, 64) (S(j+1) is then
+  // issued only after PV(j), which reads P, in the MMA thread's in-order pipeline).
+  static constexpr bool kAliasP = D == 128;
+  static constexpr int kColP = kAliasP ? 0 : 128;
+  static constexpr int kColO = kAliasP ? 128 : 192;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 struct PairBars {
@@ -126,7 +138,7 @@ __device__ __forceinline__ uint4 pack8(const float* p) {
 
 __device__ __forceinline__ bool aborted(volatile int* f) { return *f != 0; }
 
-template <typename T>
+template <typename T, int HD>
 __global__ void __launch_bounds__(320, 1)
 prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const __grid_constant__ CUtensorMap tmap_k,
@@ -138,7 +150,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const int32_t* __restrict__ seq_lens_k, int H, int group, int num_blocks,
                     int max_blocks, float scale_log2, int run8_ok, int n_split,
                     float* __restrict__ part_o, float2* __restrict__ part_ml, int* status) {
-  using Cfg = PairCfg;
+  using Cfg = PairCfg<HD>;
   constexpr int D = Cfg::D;
   constexpr int NS = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -229,12 +241,12 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tma_prefetch_desc(&tmap_v);
       tma_prefetch_desc(&tmap_k8);
       tma_prefetch_desc(&tmap_v8);
-      mbar_arrive_expect_tx(&bars->q_full, (two ? 2 : 1) * Cfg::kTileBytes);
+      mbar_arrive_expect_tx(&bars->q_full, (two ? 2 : 1) * Cfg::kQBytes);
       const uint64_t pol_q = l2_policy_evict_first();
-      tma_load_3d(smem + Cfg::kOffQ, &tmap_q, &bars->q_full, 0, g * group, q_begin + t0, pol_q);
-      if (two)
-        tma_load_3d(smem + Cfg::kOffQ + Cfg::kTileBytes, &tmap_q, &bars->q_full, 0, g * group,
-                    q_begin + t0 + tq, pol_q);
+      for (int qi = 0; qi < (two ? 2 : 1); ++qi)
+        for (int sb = 0; sb < Cfg::kSub; ++sb)
+          tma_load_3d(smem + Cfg::kOffQ + qi * Cfg::kQBytes + sb * Cfg::kSubBytes, &tmap_q,
+                      &bars->q_full, sb * 64, g * group, q_begin + t0 + qi * tq, pol_q);
     }
     auto load_id = [&](int jt) -> int {
       const int blk = 8 * jt + (lane & 7);
@@ -262,18 +274,27 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       if (j + 1 < n_load) id_next = load_id(j0 + j + 1);
       const int id0 = __shfl_sync(0xffffffffu, id, 0);
       const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & 7));
-      if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kTileBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kKVBytes);
       __syncwarp();
-      uint8_t* kst = smem + Cfg::kOffKV + st * 2 * Cfg::kTileBytes;
+      uint8_t* kst = smem + Cfg::kOffKV + st * 2 * Cfg::kKVBytes;
       if (run8) {
         if (lane == 0) {
-          tma_load_4d(kst, &tmap_k8, &bars->kv_full[st], 0, g, 0, id0, pol_kv);
-          tma_load_4d(kst + Cfg::kTileBytes, &tmap_v8, &bars->kv_full[st], 0, g, 0, id0, pol_kv);
+#pragma unroll
+          for (int sb = 0; sb < Cfg::kSub; ++sb) {
+            tma_load_4d(kst + sb * Cfg::kSubBytes, &tmap_k8, &bars->kv_full[st], sb * 64, g, 0,
+                        id0, pol_kv);
+            tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kSubBytes, &tmap_v8, &bars->kv_full[st],
+                        sb * 64, g, 0, id0, pol_kv);
+          }
         }
       } else if (lane < 8) {
-        tma_load_4d(kst + lane * 2048, &tmap_k, &bars->kv_full[st], 0, g, 0, id, pol_kv);
-        tma_load_4d(kst + Cfg::kTileBytes + lane * 2048, &tmap_v, &bars->kv_full[st], 0, g, 0,
-                    id, pol_kv);
+#pragma unroll
+        for (int sb = 0; sb < Cfg::kSub; ++sb) {
+          tma_load_4d(kst + sb * Cfg::kSubBytes + lane * 2048, &tmap_k, &bars->kv_full[st],
+                      sb * 64, g, 0, id, pol_kv);
+          tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kSubBytes + lane * 2048, &tmap_v,
+                      &bars->kv_full[st], sb * 64, g, 0, id, pol_kv);
+        }
       }
       __syncwarp();
     }
@@ -282,20 +303,22 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (lane == 0) {
       const int nk[2] = {cnt0, cnt1};  // local tile counts
       auto issue_s = [&](int i, int st) {
-        const uint32_t q = sQ + i * Cfg::kTileBytes;
-        const uint32_t k = sKV + st * 2 * Cfg::kTileBytes;
+        const uint32_t q = sQ + i * Cfg::kQBytes;
+        const uint32_t k = sKV + st * 2 * Cfg::kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc::mma_f16(tmem + 256 * i, tc::sdesc_sw128(q + kk * 32, 16, 1024),
-                      tc::sdesc_sw128(k + kk * 32, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * Cfg::kSubBytes + (kk & 3) * 32;
+          tc::mma_f16(tmem + 256 * i, tc::sdesc_sw128(q + off, 16, 1024),
+                      tc::sdesc_sw128(k + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+        }
       };
       auto issue_pv = [&](int i, int st, bool acc) {
-        const uint32_t v = sKV + st * 2 * Cfg::kTileBytes + Cfg::kTileBytes;
-        const uint32_t tP = tmem + 256 * i + 128;
-        const uint32_t tO = tmem + 256 * i + 192;
+        const uint32_t v = sKV + st * 2 * Cfg::kKVBytes + Cfg::kKVBytes;
+        const uint32_t tP = tmem + 256 * i + Cfg::kColP;
+        const uint32_t tO = tmem + 256 * i + Cfg::kColO;
 #pragma unroll
         for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
-          tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kTileBytes, 1024),
+          tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kSubBytes, 1024),
                          kIdescO, (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->q_full, 0, status);
@@ -309,7 +332,9 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const int j = js[i];
-          if (j < nk[i] && mbar_try_wait(&bars->kv_full[j % NS], (j / NS) & 1) &&
+          // with P aliased onto S, S(j) may only follow PV(j-1), which reads P(j-1)
+          if (j < nk[i] && (!Cfg::kAliasP || jp[i] >= j) &&
+              mbar_try_wait(&bars->kv_full[j % NS], (j / NS) & 1) &&
               (j == 0 || mbar_try_wait(&bars->s_free[i], (j - 1) & 1))) {
             tc::fence_after_sync();
             issue_s(i, j % NS);
@@ -354,8 +379,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int qpos = valid ? P + tok : P + ti0;
     const uint32_t trow = uint32_t(quad * 32) << 16;
     const uint32_t tS = tmem + 256 * i + trow;
-    const uint32_t tP = tS + 128;
-    const uint32_t tO = tS + 192;
+    const uint32_t tP = tS + Cfg::kColP;
+    const uint32_t tO = tS + Cfg::kColO;
     const int nkv = i ? cnt1 : cnt0;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -541,17 +566,18 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // Combines the n_split partials of every (query-tile pair, KV head, sequence):
 // O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s.  One warp per row,
 // two head-dim columns per lane.  Units and rows the main kernel skipped are skipped.
-template <typename T>
+template <typename T, int HD>
 __global__ void __launch_bounds__(256)
 prefill_merge_kernel(T* __restrict__ out, const float* __restrict__ part_o,
                      const float2* __restrict__ part_ml, const int32_t* __restrict__ cu_seqlens_q,
                      const int32_t* __restrict__ seq_lens_k, int H, int group, int npairs,
                      int n_split, int max_blocks) {
-  constexpr int D = PairCfg::D;
+  constexpr int D = HD;
+  constexpr int kPer = D / 32;  // head-dim columns per lane
   const int r = blockIdx.z, g = blockIdx.y, pair = blockIdx.x;
   const int q_begin = cu_seqlens_q[r];
   const int nq = cu_seqlens_q[r + 1] - q_begin;
-  const int tq = PairCfg::kBM / group;
+  const int tq = 128 / group;
   const int t0 = pair * 2 * tq;
   if (t0 >= nq) return;
   const int Lk = min(seq_lens_k[r], max_blocks * kBS);
@@ -568,20 +594,25 @@ prefill_merge_kernel(T* __restrict__ out, const float* __restrict__ part_o,
       const float2 ml = part_ml[(rec0 + sp) * 256 + rr];
       if (ml.y > 0.f) M = fmaxf(M, ml.x);
     }
-    float L = 0.f, ox = 0.f, oy = 0.f;
+    float L = 0.f, acc[kPer];
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
     for (int sp = 0; sp < n_split; ++sp) {
       const int64_t prow = (rec0 + sp) * 256 + rr;
       const float2 ml = part_ml[prow];
       if (!(ml.y > 0.f)) continue;
       const float w = fast_exp2(ml.x - M);
-      const float2 o = *reinterpret_cast<const float2*>(part_o + prow * D + 2 * lane);
+      const float* o = part_o + prow * D + kPer * lane;
       L = fmaf(ml.y, w, L);
-      ox = fmaf(o.x, w, ox);
-      oy = fmaf(o.y, w, oy);
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) acc[e] = fmaf(o[e], w, acc[e]);
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* dst = out + (int64_t(q_begin) + tok) * int64_t(H) * D + int64_t(g * group + hq) * D;
-    *reinterpret_cast<uint32_t*>(dst + 2 * lane) = pack2<T>(ox * inv, oy * inv);
+    T* dst = out + (int64_t(q_begin) + tok) * int64_t(H) * D + int64_t(g * group + hq) * D +
+             kPer * lane;
+#pragma unroll
+    for (int e = 0; e < kPer; e += 2)
+      *reinterpret_cast<uint32_t*>(dst + e) = pack2<T>(acc[e] * inv, acc[e + 1] * inv);
   }
 }
 
@@ -591,13 +622,13 @@ CUtensorMapDataType tmap_dtype() {
                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-template <typename T>
+template <typename T, int HD>
 int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
                 const void* v_cache, const int32_t* bt, int64_t bt_stride, const int32_t* cu,
                 const int32_t* lk, int R, int max_seqlen_q, int total_q, int H, int Kh,
                 int num_blocks, int max_blocks, float scale, int n_split, void* workspace,
                 cudaStream_t stream) {
-  using Cfg = PairCfg;
+  using Cfg = PairCfg<HD>;
   constexpr int D = Cfg::D;
   const int group = H / Kh;
   const int tq = Cfg::kBM / group;
@@ -630,7 +661,7 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
                              box8, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  auto kern = prefill_pair_kernel<T>;
+  auto kern = prefill_pair_kernel<T, HD>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   const int npairs = pair_count(max_seqlen_q, H, Kh);
   float2* part_ml = nullptr;
@@ -648,7 +679,7 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
       device_status_ptr());
   int rc = check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
   if (rc || n_split == 1) return rc;
-  prefill_merge_kernel<T><<<dim3(npairs, Kh, R), 256, 0, stream>>>(
+  prefill_merge_kernel<T, HD><<<dim3(npairs, Kh, R), 256, 0, stream>>>(
       static_cast<T*>(out), part_o, part_ml, cu, lk, H, H / Kh, npairs, n_split, max_blocks);
   return check_launch("as_varlen_prefill_attention (split-KV merge)");
 }
@@ -664,7 +695,7 @@ int prefill_pair_splits(int R, int max_seqlen_q, int H, int Kh, int max_blocks, 
   // taken only when it is predicted 25% faster.
   constexpr double kCtaOverheadTiles = 14.5;
   const int units = pair_count(max_seqlen_q, H, Kh) * Kh * R;
-  const int tiles = (max_blocks * kBS + PairCfg::kBN - 1) / PairCfg::kBN;
+  const int tiles = (max_blocks * kBS + 127) / 128;  // KV tiles of 128 keys
   const int slots = sm_count();
   int best = 1;
   double best_cost = 0.0;
@@ -680,25 +711,26 @@ int prefill_pair_splits(int R, int max_seqlen_q, int H, int Kh, int max_blocks, 
   return best;
 }
 
-size_t prefill_pair_workspace_size(int R, int max_seqlen_q, int H, int Kh, int n_split) {
+size_t prefill_pair_workspace_size(int R, int max_seqlen_q, int H, int Kh, int D, int n_split) {
   if (n_split <= 1) return 0;
   const size_t rows = size_t(pair_count(max_seqlen_q, H, Kh)) * Kh * R * n_split * 256;
-  return align256(rows * sizeof(float2)) + align256(rows * PairCfg::D * sizeof(float));
+  return align256(rows * sizeof(float2)) + align256(rows * size_t(D) * sizeof(float));
 }
 
 int prefill_pair_launch(void* out, const void* q, int64_t q_stride, const void* k_cache,
                         const void* v_cache, const int32_t* bt, int64_t bt_stride,
                         const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int R,
-                        int max_seqlen_q, int total_q, int H, int Kh, int num_blocks,
+                        int max_seqlen_q, int total_q, int H, int Kh, int D, int num_blocks,
                         int max_blocks, float scale, int dtype, int n_split, void* workspace,
                         cudaStream_t stream) {
+#define AS_PAIR_LAUNCH(T, HD)                                                                    \
+  launch_pair<T, HD>(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,            \
+                     seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks, max_blocks, scale, \
+                     n_split, workspace, stream)
   if (dtype == AS_DTYPE_BF16)
-    return launch_pair<__nv_bfloat16>(out, q, q_stride, k_cache, v_cache, bt, bt_stride,
-                                      cu_seqlens_q, seq_lens_k, R, max_seqlen_q, total_q, H, Kh,
-                                      num_blocks, max_blocks, scale, n_split, workspace, stream);
-  return launch_pair<__half>(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
-                             seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks, max_blocks,
-                             scale, n_split, workspace, stream);
+    return D == 64 ? AS_PAIR_LAUNCH(__nv_bfloat16, 64) : AS_PAIR_LAUNCH(__nv_bfloat16, 128);
+  return D == 64 ? AS_PAIR_LAUNCH(__half, 64) : AS_PAIR_LAUNCH(__half, 128);
+#undef AS_PAIR_LAUNCH
 }
 
 }  // namespace asb

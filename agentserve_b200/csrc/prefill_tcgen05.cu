@@ -545,9 +545,9 @@ int prefill_tc_launch(void* out, const void* q, int64_t q_stride, const void* k_
 #ifndef AS_PREFILL_PAIR
 #define AS_PREFILL_PAIR 1
 #endif
-  if (AS_PREFILL_PAIR && D == 64)
+  if (AS_PREFILL_PAIR && (D == 64 || D == 128))
     return prefill_pair_launch(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
-                               seq_lens_k, R, max_seqlen_q, total_q, H, Kh, num_blocks,
+                               seq_lens_k, R, max_seqlen_q, total_q, H, Kh, D, num_blocks,
                                max_blocks, scale, dtype, n_split, workspace, stream);
   if (dtype == AS_DTYPE_BF16) {
     using T = __nv_bfloat16;

@@ -208,7 +208,7 @@ AS_API int as_varlen_prefill_attention(void* out, const void* q, int64_t q_strid
                                 int32_t dtype, as_stream_t stream);
 
 /* Same computation with split-KV (same reference interface, llama.py:128-186): for
- * head_dim 64 in bf16/f16 the key range of every query tile pair can be divided over
+ * head_dim 64 or 128 in bf16/f16 the key range of every query tile pair can be divided over
  * num_splits CTAs, whose partial results (fp32) go to `workspace` and are combined by
  * a second kernel on the same stream.  This fills the GPU when few sequences are
  * prefilled at once (the reference prefills one request per call, engine.py:228-229).

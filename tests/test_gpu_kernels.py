@@ -352,24 +352,25 @@ def test_prefill_consecutive_block_runs(D):
     status_ok()
 
 
-@pytest.mark.parametrize("num_splits", [2, 3, 5, 8, 16])
-def test_prefill_split_kv_vs_oracle(num_splits):
+@pytest.mark.parametrize("num_splits,D", [(2, 64), (3, 64), (5, 64), (8, 64), (16, 64),
+                                          (2, 128), (5, 128)])
+def test_prefill_split_kv_vs_oracle(num_splits, D):
     """Split-KV prefill (head_dim 64): each query-tile pair's key range divided over
     CTAs and merged; sequences shorter than the split count (empty splits), prefixes
     that end mid-tile and causal tails inside the last splits."""
     num_cached = [3000, 0, 37, 700, 16, 1]
     num_new = [90, 5, 64, 200, 1, 129]
-    tables, kp, vp, q, cu, lens = prefill_case(num_cached, num_new, 32, 8, 64, torch.bfloat16,
+    tables, kp, vp, q, cu, lens = prefill_case(num_cached, num_new, 32, 8, D, torch.bfloat16,
                                                seed=90 + num_splits)
     bt = padded(tables).to(DEV)
-    need = ops.prefill_workspace_bytes(len(lens), max(num_new), 32, 8, 64, bt.shape[1],
+    need = ops.prefill_workspace_bytes(len(lens), max(num_new), 32, 8, D, bt.shape[1],
                                        num_splits)
     assert need > 0
     ws = torch.empty(need, dtype=torch.uint8, device=DEV)
     out = ops.varlen_prefill_attention(q.to(DEV), kp.to(DEV), vp.to(DEV), bt,
                                        torch.from_numpy(cu).to(DEV),
                                        torch.tensor(lens, dtype=torch.int32, device=DEV),
-                                       max(num_new), 0.125, num_splits=num_splits,
+                                       max(num_new), D ** -0.5, num_splits=num_splits,
                                        workspace=ws).cpu()
     ref = OA.prefill_attention_from_pool(q.float(), kp.float(), vp.float(), tables, cu, lens)
     torch.testing.assert_close(out.float(), ref, rtol=0, atol=ATOL_LOWP)

@@ -345,3 +345,41 @@ def test_zero_copy_prefix_sharing_prefill_and_decode():
         a.free(r)
     a.release_blocks(prefix)
     assert a.num_used_blocks() == 0
+
+
+def test_chunked_prefill_equals_one_shot():
+    """Chunked prefill through forward_prefill_paged (each chunk attends to the chunks
+    already in the pool, num_cached = tokens done so far) gives the one-shot prefill's
+    last-token logits and pool contents; two requests advance chunk by chunk in the
+    same batched calls."""
+    cfg = ModelConfig(**PAGED_CFG)
+    m = b200_model(cfg, torch.float32, fused=True)
+    g = torch.Generator().manual_seed(13)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,), generator=g).tolist() for n in (300, 170)]
+    mk = lambda: DeviceBlockAllocator(64, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                                      dtype=torch.float32, device=DEV)
+    one, chunked = mk(), mk()
+    rids = ["a", "b"]
+    for a in (one, chunked):
+        for r, p in zip(rids, prompts):
+            a.allocate(r, a.blocks_needed(len(p)))
+    want = m.forward_prefill_paged(prompts, [0, 0], one, rids)
+    done = [0, 0]
+    last = {}
+    while any(d < len(p) for d, p in zip(done, prompts)):
+        sel = [i for i, (d, p) in enumerate(zip(done, prompts)) if d < len(p)]
+        chunks = [prompts[i][done[i]:done[i] + 128] for i in sel]
+        lg = m.forward_prefill_paged([prompts[i][:done[i]] + c for i, c in zip(sel, chunks)],
+                                     [done[i] for i in sel], chunked, [rids[i] for i in sel])
+        for k, i in enumerate(sel):
+            done[i] += len(chunks[k])
+            if done[i] == len(prompts[i]):
+                last[i] = lg[k]
+    for i in range(len(prompts)):
+        torch.testing.assert_close(last[i], want[i], rtol=0, atol=2e-4)
+    for r, p in zip(rids, prompts):
+        for li in range(cfg.n_layers):
+            k1, v1 = one.gather_kv(r, len(p), li)
+            k2, v2 = chunked.gather_kv(r, len(p), li)
+            torch.testing.assert_close(k2, k1, rtol=0, atol=1e-5)
+            torch.testing.assert_close(v2, v1, rtol=0, atol=1e-5)
