@@ -227,13 +227,14 @@ def prefill_flops(num_cached, num_new, H, D):
     return sum(4 * H * D * (T * P + T * (T + 1) // 2) for P, T in zip(num_cached, num_new))
 
 
-def measure_prefill(dev, reps: int = 10):
+def measure_prefill(dev, reps: int = 10, D: int = 64):
     """The prefix-cache workload's prefill shape (a 14,336-token cached prefix plus a
-    600-token suffix, Llama-3.2-1B attention geometry, bf16), as the reference runs it
-    (one request per call) and as a varlen batch of 8 such requests, on the varlen
-    prefill kernel alone; CUDA events around `reps` launches."""
+    600-token suffix, 32/8 heads of head_dim D: 64 is the Llama-3.2-1B geometry, 128 the
+    8B one, bf16), as the reference runs it (one request per call) and as a varlen batch
+    of 8 such requests, on the varlen prefill kernel alone; CUDA events around `reps`
+    launches."""
     from agentserve_b200 import ops
-    H, Kh, D = 32, 8, 64
+    H, Kh = 32, 8
     res = {}
     for tag, R in (("1x", 1), ("8x", 8)):
         num_cached, num_new = [14336] * R, [600] * R
@@ -428,6 +429,7 @@ def run_b200(args):
     achieved = abytes / (attn_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
     pf = measure_prefill(dev) if not args.no_prefill and tp == 1 else None
+    pf128 = measure_prefill(dev, D=128) if not args.no_prefill and tp == 1 else None
     bits = ops.device_status(clear=True)
 
     if world > 1:
@@ -479,7 +481,11 @@ def run_b200(args):
                              "peak": measured_bf16_peak()[0], "unit": "TFLOP/s",
                              "frac": pf["8x"]["tflops"] / measured_bf16_peak()[0],
                              "peak_source": measured_bf16_peak()[1] + " bf16_tflops (burst)"},
-                "one_request": pf["1x"], "eight_requests": pf["8x"]},
+                "one_request": pf["1x"], "eight_requests": pf["8x"],
+                "head_dim_128": {"note": "same shape with the 8B geometry's head_dim 128 "
+                                         "(32/8 heads)", "one_request": pf128["1x"],
+                                 "eight_requests": pf128["8x"],
+                                 "frac": pf128["8x"]["tflops"] / measured_bf16_peak()[0]}},
             "clocks": clk, "device_status": bits,
         }
         if world == 1 and not args.no_cpu_baseline:
