@@ -480,8 +480,12 @@ class B200LlamaModel(nn.Module):
         return g.run(tokens, seq_lens, rows)
 
     def release_decode_graphs(self) -> None:
-        """Drop every cached decode graph (e.g. before destroying a process group whose
-        all-reduce the graphs captured)."""
+        """Drop every cached decode graph now (e.g. before destroying a process group
+        whose all-reduce the graphs captured: a live graph holding NCCL work keeps the
+        group's teardown waiting)."""
+        torch.cuda.synchronize()
+        for g in self._graphs.values():
+            g.release()
         self._graphs.clear()
         self._graph_pool = None
 
@@ -500,14 +504,19 @@ class _PagedStepGraph:
         self.copied = torch.cuda.Event()
         self.ws = ops.new_decode_workspace(B, model.H, model.Kh, model.D, max_blocks, bps, dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-
-        def body():
-            return model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
-                                      allocator, max_blocks, bps, ws=self.ws)
-
-        self._body = body
+        self.model, self.max_blocks, self.bps = model, max_blocks, bps
         self._pool = pool
         self.logits: Optional[torch.Tensor] = None
+
+    def _body(self) -> torch.Tensor:
+        return self.model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
+                                       self.allocator, self.max_blocks, self.bps, ws=self.ws)
+
+    def release(self) -> None:
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
+        self.logits = None
 
     def _stage(self, tokens, seq_lens, rows) -> None:
         self.copied.synchronize()  # the previous call's copy has left the pinned buffer
@@ -603,3 +612,11 @@ class DecodeGraph:
     def replay(self) -> torch.Tensor:
         self.graph.replay()
         return self.next_tokens
+
+    def release(self) -> None:
+        """Free the captured graph now (before destroying a process group whose
+        all-reduce it captured)."""
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None

@@ -18,6 +18,7 @@ One JSON line on rank 0:
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -385,6 +386,7 @@ def run_b200(args):
     # ---------------- end to end through forward_decode_paged with host lists
     cur = [L + args.warmup + args.steps for L in lens]
     last = graph.next_tokens.cpu().tolist()
+    graph.release()
     del graph
     torch.cuda.synchronize()
     e2e_steps = max(3, args.e2e_steps)
@@ -494,6 +496,7 @@ def run_b200(args):
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
     model.release_decode_graphs()  # they captured this group's all-reduce
+    gc.collect()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
