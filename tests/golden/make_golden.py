@@ -7,7 +7,7 @@ Run in a container where the reference (krishs0404/agentserve) is checked out:
 The default PATH is $AGENTSERVE_REFERENCE or /root/reference.  Every array
 written here comes from the reference's own code (BlockAllocator, apply_rope,
 precompute_rope_freqs, LlamaModel.forward / forward_decode_batch /
-forward_decode_paged), on seeded inputs that the tests regenerate.  Large inputs
+forward_decode_paged, sample at temperature 0), on seeded inputs that the tests regenerate.  Large inputs
 are not stored: the tests rebuild them from the same seeds and check the stored
 sha256 of their bytes first.  The tests never import the reference.
 """
@@ -42,6 +42,14 @@ def import_reference(path: str):
     import agentserve.model.config as config  # noqa: F401
     import agentserve.model.llama as llama  # noqa: F401
     return cache, config, llama
+
+
+def gen_greedy(path: str, out):
+    """The reference's sampler at temperature 0 (sampling.py:46-58)."""
+    import agentserve.engine.sampling as sampling
+    x32, xbf = S.greedy_logits()
+    out["greedy_tokens_f32"] = sampling.sample(x32, temperature=0.0).numpy()
+    out["greedy_tokens_bf16"] = sampling.sample(xbf, temperature=0.0).numpy()
 
 
 def gen_rope(llama, out):
@@ -195,6 +203,7 @@ def main():
     gen_cache(cache, out)
     gen_decode_cfg1(cache, out)
     gen_models(config_mod, llama, cache, out)
+    gen_greedy(args.reference, out)
     path = HERE / "reference_golden.npz"
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({path.stat().st_size / 1e6:.2f} MB, {len(out)} arrays)")

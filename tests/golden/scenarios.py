@@ -65,3 +65,19 @@ def model_scenario(tag: str, cfg):
     prompt = torch.randint(3, V, (37,), generator=g).tolist()
     batch_prompts = [torch.randint(3, V, (n,), generator=g).tolist() for n in (4, 6, 5, 19)]
     return dict(prompt=prompt, batch_prompts=batch_prompts)
+
+
+def greedy_logits():
+    """Seeded logits for greedy sampling (sampling.py:46-58): NaN, +-inf, a tie, an
+    all -inf row and values past the 1e4 the reference maps +inf to.  Returns the fp32
+    logits and their bf16 rounding."""
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(6, 3000, generator=g) * 4
+    x[0, 11] = float("nan")
+    x[0, 1200] = float("inf")
+    x[1, :] = -float("inf")
+    x[2, 5] = x[2, 2999] = x[2].max() + 2.0
+    x[3, 7] = 2.0e4            # finite and above +inf's replacement (1e4)
+    x[3, 8] = float("inf")
+    x[4, :] = float("nan")     # all NaN -> all 0 -> index 0
+    return x, x.to(torch.bfloat16)

@@ -471,6 +471,14 @@ def test_greedy_argmax_matches_reference_sampling(dtype, B, V):
     status_ok()
 
 
+def test_greedy_argmax_matches_reference_golden(golden):
+    """The kernel reproduces the tokens the reference's own sampler chose."""
+    x32, xbf = S.greedy_logits()
+    assert ops.greedy_argmax(x32.to(DEV)).cpu().tolist() == golden["greedy_tokens_f32"].tolist()
+    assert ops.greedy_argmax(xbf.to(DEV)).cpu().tolist() == golden["greedy_tokens_bf16"].tolist()
+    status_ok()
+
+
 # ---------------------------------------------------------------- block copy
 def test_block_copy_gather_and_seed_bit_exact():
     g = torch.Generator().manual_seed(6)

@@ -132,3 +132,12 @@ def test_oracle_model_matches_reference(golden):
             last = [int(t) for t in lg.argmax(-1)]
             assert last == golden[f"{tag}_paged_tokens"][step].tolist()
             lens = [x + 1 for x in lens]
+
+
+def test_oracle_greedy_matches_reference_sampler(golden):
+    """The oracle's greedy branch equals the reference's sample(temperature=0) on
+    logits with NaN, +-inf, ties and values above the +inf replacement."""
+    from oracle.model import greedy
+    x32, xbf = S.greedy_logits()
+    assert greedy(x32).numpy().tolist() == golden["greedy_tokens_f32"].tolist()
+    assert greedy(xbf).numpy().tolist() == golden["greedy_tokens_bf16"].tolist()
