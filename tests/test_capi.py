@@ -92,3 +92,31 @@ def test_zero_sized_calls_are_no_ops(lib):
     assert lib.as_varlen_prefill_attention(None, None, 2048, None, None, None, 8, None, None, 0,
                                            0, 0, 32, 8, 64, 16, 10, 8, 0.125, N.AS_DTYPE_BF16,
                                            None) == N.AS_OK
+
+
+def test_new_entry_points_host_checks(lib):
+    """Workspace-size arithmetic and argument checks of the split-KV prefill, the
+    small-batch projection and the greedy sampler, all answered on the host."""
+    # split-KV prefill: 1 sequence, 16 new tokens, 32/8 heads, D=64 -> 1 pair per head;
+    # 4 forced splits -> 8 heads * 4 * 256 rows of (m, l) + D fp32 values
+    rows = 8 * 4 * 256
+    n = lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 4, N.AS_DTYPE_BF16)
+    assert n == -(-rows * 8 // 256) * 256 + -(-rows * 64 * 4 // 256) * 256
+    assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 1, N.AS_DTYPE_BF16) == 0
+    assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 4, N.AS_DTYPE_F32) == 0
+    assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 96, 1900, 4, N.AS_DTYPE_BF16) == 0
+    # projection: counters for ceil(N/128) tiles rounded to 256 B, then fp32 [M, N]
+    assert lib.as_linear_small_m_workspace_size(64, 3072) == 256 + 64 * 3072 * 4
+    assert lib.as_linear_small_m_workspace_size(300, 3072) == 0
+    rc = lib.as_linear_small_m(None, 16, None, 16, None, 4, 16, 16, N.AS_DTYPE_F32, None, 0, None)
+    assert rc == N.AS_ERR_UNSUPPORTED
+    rc = lib.as_linear_small_m(None, 16, None, 16, None, 300, 16, 16, N.AS_DTYPE_BF16, None, 0,
+                               None)
+    assert rc == N.AS_ERR_UNSUPPORTED and "M > 256" in N.last_error()
+    # greedy: keys [rows] u64 and counters [rows] i32, each rounded to 256 B
+    assert lib.as_greedy_workspace_size(64) == 512 + 256
+    rc = lib.as_greedy_argmax(None, None, 100, 4, 100, N.AS_DTYPE_BF16, None, 0, None)
+    assert rc == N.AS_ERR_INVALID_ARG  # null pointers
+    rc = lib.as_greedy_argmax(None, None, 50, 4, 100, N.AS_DTYPE_BF16, None, 0, None)
+    assert rc == N.AS_ERR_INVALID_ARG  # row stride < vocab
+    assert lib.as_greedy_argmax(None, None, 100, 0, 100, N.AS_DTYPE_BF16, None, 0, None) == N.AS_OK
