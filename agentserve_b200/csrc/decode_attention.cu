@@ -90,15 +90,18 @@ __device__ void splitk_finish(const DecodeWorkspace& ws, T* __restrict__ out, in
                               int Kh, int D, int group, int nsplit, int max_splits, int os_h,
                               int os_d) {
   __shared__ int s_last;
-  __threadfence();
+  // The barrier orders every thread's partial stores before thread 0's fence, which
+  // (cumulatively) publishes them before the counter update; the last CTA's thread 0
+  // fences again before the barrier that releases the merge reads.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const int prev = atomicAdd(ws.counters + b * Kh + g, 1);
     s_last = (prev == nsplit - 1);
+    if (s_last) __threadfence();
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   for (int idx = threadIdx.x; idx < group * D; idx += blockDim.x) {
     const int hl = idx / D;
     const int d = idx - hl * D;
