@@ -538,7 +538,11 @@ class _PagedStepGraph:
             torch.cuda.current_stream().wait_stream(s)
             torch.cuda.synchronize()
             self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph, pool=self._pool):
+            # relaxed: a library kernel first used inside the capture (lazy module
+            # loading, e.g. a cuBLAS algorithm the warm-up did not pick) must not
+            # invalidate it
+            with torch.cuda.graph(self.graph, pool=self._pool, stream=s,
+                                  capture_error_mode="relaxed"):
                 self.logits = self._body()
         self.graph.replay()
         return self.logits.clone()
@@ -600,7 +604,7 @@ class DecodeGraph:
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with torch.cuda.graph(self.graph, stream=s, capture_error_mode="relaxed"):
             self._body()
         torch.cuda.synchronize()
 
