@@ -1,7 +1,7 @@
 // (4) Varlen prefill attention over cached prefix blocks + new tokens: entry point
 // and the CUDA-core kernel used for fp32 and for head dims the tensor-core kernel
 // does not cover.  The bf16/fp16 tensor-core kernel (tcgen05 + TMEM) lives in
-// prefill_tcgen05.cu.
+// prefill_pair.cu.
 //
 // Semantics follow LlamaAttention.forward with a cached prefix
 // (agentserve/model/llama.py:128-186): new token i of a sequence whose first P

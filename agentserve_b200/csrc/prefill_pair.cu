@@ -1,9 +1,10 @@
 // (4) Varlen prefill attention, head_dim 64 and 128: two query tiles per CTA sharing
 // every K/V tile, P kept in tensor memory.
 //
-// Semantics as in prefill_tcgen05.cu (LlamaAttention.forward over a cached prefix,
-// agentserve/model/llama.py:128-186): token i of a sequence with P cached tokens
-// attends to keys 0..P+i, K/V read in place from the paged pool.
+// Semantics: LlamaAttention.forward over a cached prefix (agentserve/model/llama.py:
+// 128-186): token i of a sequence with P cached tokens attends to keys 0..P+i (prefix
+// unmasked, new tokens causal, the mask of llama.py:171-180), K/V read in place from
+// the paged pool.
 //
 // CTA = (pair of query tiles, KV head g, sequence).  Query tile i (i = 0, 1) holds
 // 128 rows = tq tokens x the `group` query heads of KV head g.  Per KV tile of 128
@@ -731,6 +732,34 @@ int prefill_pair_launch(void* out, const void* q, int64_t q_stride, const void* 
     return D == 64 ? AS_PAIR_LAUNCH(__nv_bfloat16, 64) : AS_PAIR_LAUNCH(__nv_bfloat16, 128);
   return D == 64 ? AS_PAIR_LAUNCH(__half, 64) : AS_PAIR_LAUNCH(__half, 128);
 #undef AS_PAIR_LAUNCH
+}
+
+namespace {
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+}  // namespace
+
+bool prefill_tc_supported(int dtype, int H, int Kh, int D, const void* q, int64_t q_stride,
+                          const void* k_cache, const void* v_cache, const void* out) {
+  if (dtype != AS_DTYPE_BF16 && dtype != AS_DTYPE_F16) return false;
+  if (D != 64 && D != 128) return false;
+  const int group = H / Kh;
+  if (group < 1 || group > 128 || 128 % group != 0) return false;  // whole tokens per tile
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out)) return false;
+  if ((q_stride * 2) % 16 != 0) return false;
+  return true;
+}
+
+int prefill_tc_launch(void* out, const void* q, int64_t q_stride, const void* k_cache,
+                      const void* v_cache, const int32_t* bt, int64_t bt_stride,
+                      const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int R,
+                      int max_seqlen_q, int total_q, int H, int Kh, int D, int num_blocks,
+                      int max_blocks, float scale, int dtype, int n_split, void* workspace,
+                      cudaStream_t stream) {
+  if (max_seqlen_q <= 0) return AS_OK;
+  if (R > 65535) return fail(AS_ERR_INVALID_ARG, "as_varlen_prefill_attention: too many sequences");
+  return prefill_pair_launch(out, q, q_stride, k_cache, v_cache, bt, bt_stride, cu_seqlens_q,
+                             seq_lens_k, R, max_seqlen_q, total_q, H, Kh, D, num_blocks,
+                             max_blocks, scale, dtype, n_split, workspace, stream);
 }
 
 }  // namespace asb

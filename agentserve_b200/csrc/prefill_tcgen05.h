@@ -1,4 +1,5 @@
-// Tensor-core (tcgen05 + TMEM) varlen prefill attention: internal interface.
+// Tensor-core (tcgen05 + TMEM) varlen prefill attention (prefill_pair.cu): internal
+// interface.
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
