@@ -12,10 +12,10 @@
 //              (X rows >= M read as zeros), 4-stage ring;
 //   warp 1     MMA issuer (one thread), commits each stage back to the producer;
 //   warps 2-5  epilogue, one TMEM lane (= weight row n) per thread: with one split it
-//              stores Y directly; with several it adds its partial into an fp32
-//              accumulator with global reductions, and the last CTA of the N tile
-//              (arrival counter) converts the tile to Y and zeroes the accumulator and
-//              the counter again, so the workspace is zero between calls.
+//              stores Y directly; with several it stores its fp32 partial tile (which
+//              stays in L2), and the last CTA of the N tile (arrival counter) sums the
+//              splits in a fixed order into Y and resets the counter, so results are
+//              deterministic and the counters are zero between calls.
 // Every wait is bounded (status bit 4).
 #include <type_traits>
 
@@ -26,12 +26,23 @@
 namespace asb {
 
 constexpr int kLinTileN = 128;
-// [ceil(N/128)] int arrival counters, rounded to 256 bytes, then fp32 [M, N]
+constexpr int kLinMaxSplits = 16;
+// K splits: enough CTAs for two per SM (at least 2 K steps each, at most 16 splits)
+int linear_max_splits(int N) {
+  const int n_tiles = (N + kLinTileN - 1) / kLinTileN;
+  const int want = (2 * sm_count() + n_tiles - 1) / n_tiles;
+  return want < 1 ? 1 : (want > kLinMaxSplits ? kLinMaxSplits : want);
+}
+// [ceil(N/128)] int arrival counters, rounded to 256 bytes, then fp32 partial sums
+// [splits, N, M4] (M4 = M rounded up to 4: one weight row's batch column is 16-byte
+// vectors)
+inline int round4(int m) { return (m + 3) / 4 * 4; }
 size_t linear_counter_bytes(int N) {
   return (size_t((N + kLinTileN - 1) / kLinTileN) * sizeof(int) + 255) / 256 * 256;
 }
 size_t linear_workspace_bytes(int M, int N) {
-  return linear_counter_bytes(N) + size_t(M) * N * sizeof(float);
+  return linear_counter_bytes(N) +
+         size_t(linear_max_splits(N)) * N * round4(M) * sizeof(float);
 }
 
 namespace {
@@ -160,6 +171,7 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full, 0, status)) &&
                     !aborted_flag(abort_flag);
+    const int M4 = (M + 3) / 4 * 4;
     if (ok) {
       tc::fence_after_sync();
       for (int c = 0; c < Mpad; c += 16) {
@@ -167,16 +179,18 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
         tc::ld_32x32b_x16(trow + c, v);
         tc::wait_ld();
         if (n < N) {
+          if (k_splits == 1) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int m = c + e;
-            if (m < M) {
-              const float f = __uint_as_float(v[e]);
-              if (k_splits == 1)
-                y[int64_t(m) * y_stride + n] = Elem<T>::from_f32(f);
-              else
-                atomicAdd(acc + int64_t(m) * N + n, f);
-            }
+            for (int e = 0; e < 16; ++e)
+              if (c + e < M) y[int64_t(c + e) * y_stride + n] = Elem<T>::from_f32(__uint_as_float(v[e]));
+          } else {  // this split's partial column, kept in L2 for the finishing CTA
+            float* dst = acc + (int64_t(split) * N + n) * M4 + c;
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              if (c + e < M4)
+                __stcg(reinterpret_cast<float4*>(dst + e),
+                       make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                                   __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
           }
         }
       }
@@ -194,10 +208,26 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
       if (bars->is_last) {
         __threadfence();
         if (n < N) {
-          for (int m = 0; m < M; ++m) {
-            float* a = acc + int64_t(m) * N + n;
-            y[int64_t(m) * y_stride + n] = Elem<T>::from_f32(__ldcg(a));
-            *a = 0.f;
+          for (int c = 0; c < M4; c += 16) {  // 16 batch rows at a time, vector loads
+            float sum[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sum[e] = 0.f;
+            for (int sp = 0; sp < k_splits; ++sp) {  // fixed order: deterministic result
+              const float* src = acc + (int64_t(sp) * N + n) * M4 + c;
+#pragma unroll
+              for (int e = 0; e < 16; e += 4) {
+                if (c + e < M4) {
+                  const float4 p = __ldcg(reinterpret_cast<const float4*>(src + e));
+                  sum[e] += p.x;
+                  sum[e + 1] += p.y;
+                  sum[e + 2] += p.z;
+                  sum[e + 3] += p.w;
+                }
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < M) y[int64_t(c + e) * y_stride + n] = Elem<T>::from_f32(sum[e]);
           }
         }
         if (threadIdx.x == 64) counters[n_tile] = 0;
@@ -219,12 +249,9 @@ CUtensorMapDataType tmap_dtype() {
                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-int choose_splits(int n_tiles, int k_steps, int Mpad) {
-  // fill every SM (two CTAs each when shared memory allows) with >= 2 K steps per CTA
-  const int per_sm = 2 * smem_bytes(Mpad) <= 227 * 1024 ? 2 : 1;
-  const int want = (sm_count() * per_sm + n_tiles - 1) / n_tiles;
-  int s = want < 1 ? 1 : want;
-  const int cap = k_steps / 2 > 0 ? k_steps / 2 : 1;
+int choose_splits(int N, int k_steps) {
+  const int s = linear_max_splits(N);
+  const int cap = k_steps / 2 > 0 ? k_steps / 2 : 1;  // at least 2 K steps per CTA
   return s > cap ? cap : s;
 }
 
@@ -235,7 +262,7 @@ int launch_linear(void* y, int64_t y_stride, const void* x, int64_t x_stride, co
   const int Mpad = pad_m(M);
   const int n_tiles = (N + kTileN - 1) / kTileN;
   const int k_steps = (K + kTileK - 1) / kTileK;
-  int k_splits = choose_splits(n_tiles, k_steps, Mpad);
+  int k_splits = choose_splits(N, k_steps);
   const size_t need = linear_workspace_bytes(M, N);
   if (k_splits > 1 && (!workspace || workspace_bytes < need)) k_splits = 1;
   CUtensorMap mw, mx;

@@ -203,9 +203,9 @@ class B200LlamaModel(nn.Module):
                 and x.dtype in (torch.bfloat16, torch.float16)):
             if self._lin_ws is None:  # fixed size: CUDA graphs keep its address
                 c = self.config
-                max_n = max(self.H * self.D + 2 * self.Kh * self.D, c.hidden_dim,
-                            2 * c.intermediate_size)
-                self._lin_ws = ops.new_linear_workspace(ops.LINEAR_MAX_M, max_n, x.device)
+                widths = [self.H * self.D + 2 * self.Kh * self.D, c.hidden_dim,
+                          2 * c.intermediate_size]
+                self._lin_ws = ops.new_linear_workspace(ops.LINEAR_MAX_M, widths, x.device)
             return ops.linear_small_m(x, w, workspace=self._lin_ws)
         return F.linear(x, w)
 

@@ -283,9 +283,12 @@ def linear_workspace_bytes(max_m: int, max_n: int) -> int:
     return int(N.load().as_linear_small_m_workspace_size(max_m, max_n))
 
 
-def new_linear_workspace(max_m: int, max_n: int, device) -> torch.Tensor:
-    """Zero-filled; the library leaves it zero after every call."""
-    return torch.zeros(linear_workspace_bytes(max_m, max_n), dtype=torch.uint8, device=device)
+def new_linear_workspace(max_m: int, ns, device) -> torch.Tensor:
+    """Zero-filled workspace for every output width in `ns` (an int or a list) at up to
+    max_m rows; the library keeps its arrival counters zero between calls."""
+    ns = [ns] if isinstance(ns, int) else list(ns)
+    need = max(linear_workspace_bytes(max_m, n) for n in ns)
+    return torch.zeros(need, dtype=torch.uint8, device=device)
 
 
 def linear_small_m(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,

@@ -105,8 +105,10 @@ def test_new_entry_points_host_checks(lib):
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 1, N.AS_DTYPE_BF16) == 0
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 4, N.AS_DTYPE_F32) == 0
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 96, 1900, 4, N.AS_DTYPE_BF16) == 0
-    # projection: counters for ceil(N/128) tiles rounded to 256 B, then fp32 [M, N]
-    assert lib.as_linear_small_m_workspace_size(64, 3072) == 256 + 64 * 3072 * 4
+    # projection: counters for ceil(N/128) tiles rounded to 256 B, then fp32 partials
+    # [splits, N, M rounded to 4]; without a GPU the SM count defaults to 148: 24 tiles
+    # -> 13 splits
+    assert lib.as_linear_small_m_workspace_size(64, 3072) == 256 + 13 * 64 * 3072 * 4
     assert lib.as_linear_small_m_workspace_size(300, 3072) == 0
     rc = lib.as_linear_small_m(None, 16, None, 16, None, 4, 16, 16, N.AS_DTYPE_F32, None, 0, None)
     assert rc == N.AS_ERR_UNSUPPORTED
