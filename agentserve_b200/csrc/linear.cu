@@ -12,11 +12,14 @@
 //              (X rows >= M read as zeros), 4-stage ring;
 //   warp 1     MMA issuer (one thread), commits each stage back to the producer;
 //   warps 2-5  epilogue, one TMEM lane (= weight row n) per thread: with one split it
-//              stores Y directly; with several it stores its fp32 partial tile (which
-//              stays in L2), and the last CTA of the N tile (arrival counter) sums the
-//              splits in a fixed order into Y and resets the counter, so results are
-//              deterministic and the counters are zero between calls.
-// Every wait is bounded (status bit 4).
+//              stores Y directly; with several it copies its fp32 partial tile into
+//              its own shared memory (over the drained stage ring).
+// The K splits of one N tile form a thread-block cluster (2, 4 or 8 CTAs): after a
+// cluster barrier, member r sums rows [r*128/splits, (r+1)*128/splits) of every
+// member's partial through distributed shared memory, in member order (deterministic),
+// and a second cluster barrier keeps the partials alive until all reads are done.  No
+// global workspace, no atomics.  Every mbarrier wait is bounded (status bit 4); every
+// thread of every member reaches both cluster barriers on every path.
 #include <type_traits>
 
 #include "common.cuh"
@@ -24,52 +27,52 @@
 #include "tcgen05.cuh"
 
 namespace asb {
-
-constexpr int kLinTileN = 128;
-constexpr int kLinMaxSplits = 16;
-// K splits: enough CTAs for two per SM (at least 2 K steps each, at most 16 splits)
-int linear_max_splits(int N) {
-  const int n_tiles = (N + kLinTileN - 1) / kLinTileN;
-  const int want = (2 * sm_count() + n_tiles - 1) / n_tiles;
-  return want < 1 ? 1 : (want > kLinMaxSplits ? kLinMaxSplits : want);
-}
-// [ceil(N/128)] int arrival counters, rounded to 256 bytes, then fp32 partial sums
-// [splits, N, M4] (M4 = M rounded up to 4: one weight row's batch column is 16-byte
-// vectors)
-inline int round4(int m) { return (m + 3) / 4 * 4; }
-size_t linear_counter_bytes(int N) {
-  return (size_t((N + kLinTileN - 1) / kLinTileN) * sizeof(int) + 255) / 256 * 256;
-}
-size_t linear_workspace_bytes(int M, int N) {
-  return linear_counter_bytes(N) +
-         size_t(linear_max_splits(N)) * N * round4(M) * sizeof(float);
-}
-
 namespace {
 
-constexpr int kTileN = kLinTileN;
+constexpr int kTileN = 128;
 constexpr int kTileK = 64;
-#ifndef AS_LINEAR_STAGES
-#define AS_LINEAR_STAGES 4
-#endif
-constexpr int kStages = AS_LINEAR_STAGES;
+constexpr int kStages = 4;
+constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kMaxM = 256;
 constexpr int kWBytes = kTileN * 128;  // 128 rows x 64 16-bit elements
+// split partial row pitch in floats: 128 weight rows + 16, so the 8 threads of one
+// float4 load phase that span two batch rows hit different banks
+constexpr int kPartStride = kTileN + 16;
 
 struct LinBars {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full;
   uint32_t tmem_base;
-  int is_last;
   int abort;
 };
 
 __device__ __forceinline__ bool aborted_flag(volatile int* f) { return *f != 0; }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __host__ __device__ inline int pad_m(int M) { return (M + 15) / 16 * 16; }
 __host__ __device__ inline int stage_bytes(int Mpad) { return kWBytes + Mpad * 128; }
 __host__ __device__ inline int smem_bytes(int Mpad) { return kStages * stage_bytes(Mpad) + 256; }
+// the partial [M][kPartStride] fp32 reuses the stage ring
+static_assert(kMaxM * kPartStride * 4 <= kStages * (kWBytes + kMaxM * 128),
+              "stage ring too small for the split partial");
 __host__ __device__ inline uint32_t tmem_cols(int Mpad) {
   return Mpad <= 32 ? 32u : (Mpad <= 64 ? 64u : (Mpad <= 128 ? 128u : 256u));
 }
@@ -78,8 +81,8 @@ template <typename T>
 __global__ void __launch_bounds__(192)
 linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ y,
-                      int64_t y_stride, float* __restrict__ acc, int* __restrict__ counters,
-                      int M, int Mpad, int N, int k_steps, int k_splits, int* status) {
+                      int64_t y_stride, int M, int Mpad, int N, int k_steps, int k_splits,
+                      int* status) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   const int n_tile = blockIdx.x;
   const int split = blockIdx.y;
@@ -89,6 +92,7 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
   const int sbytes = stage_bytes(Mpad);
 
   extern __shared__ __align__(1024) uint8_t smem[];
+  // (uniform over the cluster: every member has the same shared memory layout)
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) flag_status(status, kStatusWaitTimeout);
     return;
@@ -106,7 +110,6 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
     mbar_init(&bars->acc_full, 1);
     bars->abort = 0;
-    bars->is_last = 0;
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -166,80 +169,85 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;
+    const int row = quad * 32 + lane;  // TMEM lane = weight row of the tile
     const int n = n_tile * kTileN + row;
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full, 0, status)) &&
                     !aborted_flag(abort_flag);
-    const int M4 = (M + 3) / 4 * 4;
     if (ok) {
       tc::fence_after_sync();
+      // split partial: [m][kPartStride] fp32 over the stage ring (every MMA reading it
+      // has completed); lanes write consecutive weight rows, conflict-free
+      float* part = reinterpret_cast<float*>(smem);
       for (int c = 0; c < Mpad; c += 16) {
         uint32_t v[16];
         tc::ld_32x32b_x16(trow + c, v);
         tc::wait_ld();
-        if (n < N) {
-          if (k_splits == 1) {
+        if (k_splits == 1) {
+          if (n < N) {
 #pragma unroll
             for (int e = 0; e < 16; ++e)
               if (c + e < M) y[int64_t(c + e) * y_stride + n] = Elem<T>::from_f32(__uint_as_float(v[e]));
-          } else {  // this split's partial column, kept in L2 for the finishing CTA
-            float* dst = acc + (int64_t(split) * N + n) * M4 + c;
-#pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              if (c + e < M4)
-                __stcg(reinterpret_cast<float4*>(dst + e),
-                       make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                   __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
           }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < M) part[(c + e) * kPartStride + row] = __uint_as_float(v[e]);
         }
-      }
-    }
-    if (k_splits > 1) {
-      // Last-arriving CTA of this N tile finishes it (no spin: whoever arrives last
-      // sees the count).  Every CTA counts, so the counter always returns to zero.
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        const int old = atomicAdd(counters + n_tile, 1);
-        bars->is_last = (old == k_splits - 1);
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (bars->is_last) {
-        __threadfence();
-        if (n < N) {
-          for (int c = 0; c < M4; c += 16) {  // 16 batch rows at a time, vector loads
-            float sum[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) sum[e] = 0.f;
-            for (int sp = 0; sp < k_splits; ++sp) {  // fixed order: deterministic result
-              const float* src = acc + (int64_t(sp) * N + n) * M4 + c;
-#pragma unroll
-              for (int e = 0; e < 16; e += 4) {
-                if (c + e < M4) {
-                  const float4 p = __ldcg(reinterpret_cast<const float4*>(src + e));
-                  sum[e] += p.x;
-                  sum[e + 1] += p.y;
-                  sum[e + 2] += p.z;
-                  sum[e + 3] += p.w;
-                }
-              }
-            }
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (c + e < M) y[int64_t(c + e) * y_stride + n] = Elem<T>::from_f32(sum[e]);
-          }
-        }
-        if (threadIdx.x == 64) counters[n_tile] = 0;
       }
     }
     tc::fence_before_sync();
   }
 
-  __syncthreads();
+  __syncthreads();  // TMEM reads done
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, ncols);
+  }
+  if (k_splits > 1) {
+    // every member's partial is complete and visible after this barrier
+    cluster_sync_all();
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int rows = kTileN / k_splits;  // weight rows this member finishes
+    const int q = rows / 4;              // float4 vectors per batch row
+    const int r0 = int(rank) * rows;
+    const uint32_t base = smem_u32(smem);
+    for (int it = threadIdx.x; it < M * q; it += blockDim.x) {
+      const int m = it / q;
+      const int nl = r0 + (it - m * q) * 4;
+      const uint32_t off = base + uint32_t(m * kPartStride + nl) * 4u;
+      // all remote loads in flight before the first add
+      float4 p[kMaxSplits];
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplits; ++sp)
+        if (sp < k_splits) p[sp] = ld_dsmem_f4(mapa_shared(off, uint32_t(sp)));
+      float4 acc = p[0];
+#pragma unroll
+      for (int sp = 1; sp < kMaxSplits; ++sp) {  // member order: deterministic result
+        if (sp < k_splits) {
+          acc.x += p[sp].x;
+          acc.y += p[sp].y;
+          acc.z += p[sp].z;
+          acc.w += p[sp].w;
+        }
+      }
+      const int n0 = n_tile * kTileN + nl;
+      T* dst = y + int64_t(m) * y_stride + n0;
+      if (n0 + 3 < N && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+        uint2 pk;
+        pk.x = pack2<T>(acc.x, acc.y);
+        pk.y = pack2<T>(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(dst) = pk;
+      } else {
+        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (n0 + e < N) dst[e] = Elem<T>::from_f32(a[e]);
+      }
+    }
+    // peers may still be reading this member's partial
+    cluster_sync_all();
   }
 }
 
@@ -249,22 +257,23 @@ CUtensorMapDataType tmap_dtype() {
                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
+// K splits: a power of two <= 8 (so 128 divides evenly among the members), enough
+// CTAs for two per SM, at least 2 K steps per member.
 int choose_splits(int N, int k_steps) {
-  const int s = linear_max_splits(N);
-  const int cap = k_steps / 2 > 0 ? k_steps / 2 : 1;  // at least 2 K steps per CTA
-  return s > cap ? cap : s;
+  const int n_tiles = (N + kTileN - 1) / kTileN;
+  const int want = (2 * sm_count() + n_tiles - 1) / n_tiles;
+  int s = 1;
+  while (s * 2 <= kMaxSplits && s * 2 <= want && s * 2 <= k_steps / 2) s *= 2;
+  return s;
 }
 
 template <typename T>
 int launch_linear(void* y, int64_t y_stride, const void* x, int64_t x_stride, const void* w,
-                  int M, int N, int K, void* workspace, size_t workspace_bytes,
-                  cudaStream_t stream) {
+                  int M, int N, int K, cudaStream_t stream) {
   const int Mpad = pad_m(M);
   const int n_tiles = (N + kTileN - 1) / kTileN;
   const int k_steps = (K + kTileK - 1) / kTileK;
-  int k_splits = choose_splits(N, k_steps);
-  const size_t need = linear_workspace_bytes(M, N);
-  if (k_splits > 1 && (!workspace || workspace_bytes < need)) k_splits = 1;
+  const int k_splits = choose_splits(N, k_steps);
   CUtensorMap mw, mx;
   const uint64_t es = sizeof(T);
   {
@@ -283,15 +292,23 @@ int launch_linear(void* y, int64_t y_stride, const void* x, int64_t x_stride, co
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  int* counters = static_cast<int*>(workspace);
-  float* acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                        linear_counter_bytes(N));
   auto kern = linear_small_m_kernel<T>;
   const int smem = smem_bytes(Mpad);
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<dim3(n_tiles, k_splits), 192, smem, stream>>>(
-      mw, mx, static_cast<T*>(y), y_stride, k_splits > 1 ? acc : nullptr,
-      k_splits > 1 ? counters : nullptr, M, Mpad, N, k_steps, k_splits, device_status_ptr());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_tiles, k_splits);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = k_splits;  // the K splits of one N tile
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, mw, mx, static_cast<T*>(y), y_stride, M, Mpad, N, k_steps,
+                     k_splits, device_status_ptr());
   return check_launch("as_linear_small_m");
 }
 
@@ -300,14 +317,9 @@ int launch_linear(void* y, int64_t y_stride, const void* x, int64_t x_stride, co
 
 using namespace asb;
 
-extern "C" size_t as_linear_small_m_workspace_size(int32_t M, int32_t N) {
-  if (M <= 0 || M > kMaxM || N <= 0) return 0;
-  return linear_workspace_bytes(M, N);
-}
-
 extern "C" int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64_t x_stride,
                                  const void* w, int32_t M, int32_t N, int32_t K, int32_t dtype,
-                                 void* workspace, size_t workspace_bytes, as_stream_t stream) {
+                                 as_stream_t stream) {
   if (dtype != AS_DTYPE_BF16 && dtype != AS_DTYPE_F16)
     return fail(AS_ERR_UNSUPPORTED, "as_linear_small_m: bf16 or fp16 only");
   if (M < 0 || N <= 0 || K <= 0) return fail(AS_ERR_INVALID_ARG, "as_linear_small_m: bad sizes");
@@ -320,12 +332,8 @@ extern "C" int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15 ||
       (x_stride * 2) % 16 || (int64_t(K) * 2) % 16)
     return fail(AS_ERR_INVALID_ARG, "as_linear_small_m: x, w and their rows must be 16-byte aligned");
-  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255))
-    return fail(AS_ERR_INVALID_ARG, "as_linear_small_m: workspace not 256-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == AS_DTYPE_BF16)
-    return launch_linear<__nv_bfloat16>(y, y_stride, x, x_stride, w, M, N, K, workspace,
-                                        workspace_bytes, s);
-  return launch_linear<__half>(y, y_stride, x, x_stride, w, M, N, K, workspace, workspace_bytes,
-                               s);
+    return launch_linear<__nv_bfloat16>(y, y_stride, x, x_stride, w, M, N, K, s);
+  return launch_linear<__half>(y, y_stride, x, x_stride, w, M, N, K, s);
 }

@@ -159,10 +159,9 @@ class B200LlamaModel(nn.Module):
         self.decode_graphs: bool = True
         # True: projections of at most 256 tokens (the decode step) on the small-batch
         # tensor-core kernel (as_linear_small_m) instead of cuBLAS.  Off by default:
-        # measured slower than cuBLAS on B200 at batch 64 (split-K global reductions
-        # and per-CTA TMA weight streaming are the limits).
+        # measured slower than cuBLAS on B200 at batch 64 (the weight stream's ramp and
+        # the on-chip exchange of the K-split partials are the limits).
         self.small_batch_linear: bool = False
-        self._lin_ws: Optional[torch.Tensor] = None
         self.max_decode_graphs: int = 16
         self._graphs: "OrderedDict[tuple, _PagedStepGraph]" = OrderedDict()
         self._graph_pool = None
@@ -201,12 +200,7 @@ class B200LlamaModel(nn.Module):
     def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         if (self.small_batch_linear and x.shape[0] <= ops.LINEAR_MAX_M and x.is_cuda
                 and x.dtype in (torch.bfloat16, torch.float16)):
-            if self._lin_ws is None:  # fixed size: CUDA graphs keep its address
-                c = self.config
-                widths = [self.H * self.D + 2 * self.Kh * self.D, c.hidden_dim,
-                          2 * c.intermediate_size]
-                self._lin_ws = ops.new_linear_workspace(ops.LINEAR_MAX_M, widths, x.device)
-            return ops.linear_small_m(x, w, workspace=self._lin_ws)
+            return ops.linear_small_m(x, w)
         return F.linear(x, w)
 
     def _qkv(self, layer: _Layer, h: torch.Tensor):

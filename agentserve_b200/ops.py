@@ -279,33 +279,21 @@ def varlen_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: to
 LINEAR_MAX_M = 256
 
 
-def linear_workspace_bytes(max_m: int, max_n: int) -> int:
-    return int(N.load().as_linear_small_m_workspace_size(max_m, max_n))
-
-
-def new_linear_workspace(max_m: int, ns, device) -> torch.Tensor:
-    """Zero-filled workspace for every output width in `ns` (an int or a list) at up to
-    max_m rows; the library keeps its arrival counters zero between calls."""
-    ns = [ns] if isinstance(ns, int) else list(ns)
-    need = max(linear_workspace_bytes(max_m, n) for n in ns)
-    return torch.zeros(need, dtype=torch.uint8, device=device)
-
-
-def linear_small_m(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
-                   workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+def linear_small_m(x: torch.Tensor, w: torch.Tensor,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x [M, K] (row-strided view allowed, M <= 256) @ w[N, K]^T -> [M, N]: nn.Linear
-    without bias on the tensor cores, K split over CTAs through `workspace`."""
-    _cuda(x, w, out, workspace)
+    without bias on the tensor cores, K split over the CTAs of a cluster and reduced
+    on chip."""
+    _cuda(x, w, out)
     M, K = x.shape
     Nn = w.shape[0]
     assert w.shape[1] == K and w.is_contiguous() and x.stride(1) == 1 and x.dtype == w.dtype
     if out is None:
         out = torch.empty(M, Nn, dtype=x.dtype, device=x.device)
     assert out.stride(1) == 1
-    ws_bytes = workspace.numel() if workspace is not None else 0
     N.check(N.load().as_linear_small_m(
         _ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, Nn, K, dtype_code(x.dtype),
-        _ptr(workspace), ws_bytes, _stream(x.device)), "as_linear_small_m")
+        _stream(x.device)), "as_linear_small_m")
     return out
 
 

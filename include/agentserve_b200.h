@@ -243,18 +243,13 @@ AS_API size_t as_varlen_prefill_workspace_size(int32_t num_seqs, int32_t max_seq
 /* y[m, n] = sum_k x[m, k] * w[n, k] for m < M <= 256 (nn.Linear without bias: the
  * q/k/v, o_proj, gate/up and down projections of the decode step, llama.py:123-126,
  * 203-211, 430-431, 471), bf16/fp16, fp32 accumulation.  Row strides y_stride and
- * x_stride in elements; w is [N, K] row-major (nn.Linear.weight).  The K range is split
- * over CTAs when N/128 alone cannot fill the GPU; the fp32 partial sums then go
- * through `workspace` (as_linear_small_m_workspace_size(M, N) bytes for this device's
- * SM count, 256-byte aligned, zero on first use: its arrival counters must start at
- * zero and the library resets them — after a call that set a device status bit, zero
- * it again) and are added in a fixed order, so results are deterministic.  A NULL or
- * smaller workspace disables the split.  Calls sharing a workspace must be ordered on
- * one stream. */
-AS_API size_t as_linear_small_m_workspace_size(int32_t M, int32_t N);
+ * x_stride in elements; w is [N, K] row-major (nn.Linear.weight); x, w and their rows
+ * 16-byte aligned.  The K range is split over the CTAs of a thread-block cluster when
+ * N/128 alone cannot fill the GPU; the fp32 partial sums are added on chip in a fixed
+ * order, so results are deterministic and no workspace is needed. */
 AS_API int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64_t x_stride,
                              const void* w, int32_t M, int32_t N, int32_t K, int32_t dtype,
-                             void* workspace, size_t workspace_bytes, as_stream_t stream);
+                             as_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* (7) Greedy sampling                                                        */

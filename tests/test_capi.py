@@ -105,15 +105,9 @@ def test_new_entry_points_host_checks(lib):
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 1, N.AS_DTYPE_BF16) == 0
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 64, 1900, 4, N.AS_DTYPE_F32) == 0
     assert lib.as_varlen_prefill_workspace_size(1, 16, 32, 8, 96, 1900, 4, N.AS_DTYPE_BF16) == 0
-    # projection: counters for ceil(N/128) tiles rounded to 256 B, then fp32 partials
-    # [splits, N, M rounded to 4]; without a GPU the SM count defaults to 148: 24 tiles
-    # -> 13 splits
-    assert lib.as_linear_small_m_workspace_size(64, 3072) == 256 + 13 * 64 * 3072 * 4
-    assert lib.as_linear_small_m_workspace_size(300, 3072) == 0
-    rc = lib.as_linear_small_m(None, 16, None, 16, None, 4, 16, 16, N.AS_DTYPE_F32, None, 0, None)
+    rc = lib.as_linear_small_m(None, 16, None, 16, None, 4, 16, 16, N.AS_DTYPE_F32, None)
     assert rc == N.AS_ERR_UNSUPPORTED
-    rc = lib.as_linear_small_m(None, 16, None, 16, None, 300, 16, 16, N.AS_DTYPE_BF16, None, 0,
-                               None)
+    rc = lib.as_linear_small_m(None, 16, None, 16, None, 300, 16, 16, N.AS_DTYPE_BF16, None)
     assert rc == N.AS_ERR_UNSUPPORTED and "M > 256" in N.last_error()
     # greedy: keys [rows] u64 and counters [rows] i32, each rounded to 256 B
     assert lib.as_greedy_workspace_size(64) == 512 + 256
