@@ -115,13 +115,20 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // winds down instead of spinning forever).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Returns false (and flags the status word) if the wait ran out.
+// Returns false (and flags the status word) if the wait ran out.  The global timer
+// is slow to read, so it is first read after 256 polls (a wait that ends sooner
+// reads it never) and then every 256 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 255u) == 255u) {
+      const uint64_t now = global_timer_ns();
+      if (i == 255u)
+        t0 = now;
+      else if (now - t0 > kWaitLimitNs)
+        break;
+    }
   }
   flag_status(status, kStatusWaitTimeout);
   return false;

@@ -325,8 +325,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       bool ok = mbar_wait(&bars->q_full, 0, status);
       int js[2] = {0, 0};  // next S tile per query tile
       int jp[2] = {0, 0};  // next PV tile per query tile
-      uint64_t t_last = global_timer_ns();
-      uint32_t spin = 0;
+      uint64_t t_idle = 0;  // start of the current stretch without progress
+      uint32_t spin = 0;    // polls since the last issue
       while (ok && (jp[0] < nk[0] || jp[1] < nk[1])) {
         if (aborted(abort_flag)) break;
         bool did = false;
@@ -356,10 +356,15 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
           }
         }
         if (did) {
-          t_last = global_timer_ns();
-        } else if ((++spin & 255u) == 0u && global_timer_ns() - t_last > kWaitLimitNs) {
-          flag_status(status, kStatusWaitTimeout);
-          ok = false;
+          spin = 0;
+        } else if ((++spin & 255u) == 0u) {  // the timer is slow to read: rarely
+          const uint64_t now = global_timer_ns();
+          if (spin == 256u) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitLimitNs) {
+            flag_status(status, kStatusWaitTimeout);
+            ok = false;
+          }
         }
       }
       if (!ok) *abort_flag = 1;
