@@ -34,6 +34,12 @@ def _cuda(*ts: Optional[torch.Tensor]) -> None:
             raise RuntimeError("agentserve_b200 ops need CUDA tensors (no CPU fallback)")
 
 
+def _require(ok: bool, what: str) -> None:
+    """Argument checks raise ValueError (kept under python -O, unlike assert)."""
+    if not ok:
+        raise ValueError(what)
+
+
 def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -89,8 +95,9 @@ def pack_decode(block_tables: torch.Tensor, seq_lens: torch.Tensor,
                          torch.empty(B, dtype=torch.int32, device=dev),
                          torch.empty(B + 1, dtype=torch.int32, device=dev),
                          torch.empty(B, mb, dtype=torch.int32, device=dev))
-    assert block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32
-    assert block_tables.stride(1) == 1
+    _require(block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32,
+             "pack_decode: block_tables and seq_lens must be int32")
+    _require(block_tables.stride(1) == 1, "pack_decode: block_tables rows must be contiguous")
     N.check(N.load().as_pack_decode(
         _ptr(block_tables), block_tables.stride(0), _ptr(row_ids), _ptr(seq_lens), B, mb,
         BLOCK_SIZE, _ptr(out.positions), _ptr(out.slot_mapping), _ptr(out.seq_lens_k),
@@ -139,9 +146,11 @@ def rope_reshape_and_cache(q: Optional[torch.Tensor], k: torch.Tensor, v: torch.
         if t is not None and not _row_view_ok(t):
             raise ValueError(f"{name} must be [T, heads, D] with contiguous rows")
     if cos_sin is not None:
-        assert cos_sin.dtype == torch.float32 and cos_sin.is_contiguous()
-    assert k_cache.is_contiguous() and v_cache.is_contiguous()
-    assert k_cache.shape[1:] == (BLOCK_SIZE, Kh, D), "k_cache must be [NB, 16, Kh, D]"
+        _require(cos_sin.dtype == torch.float32 and cos_sin.is_contiguous(),
+                 "cos_sin must be a contiguous float32 table")
+    _require(k_cache.is_contiguous() and v_cache.is_contiguous(), "KV planes must be contiguous")
+    _require(k_cache.shape[1:] == (BLOCK_SIZE, Kh, D) and v_cache.shape == k_cache.shape,
+             "k_cache / v_cache must be [NB, 16, Kh, D]")
     num_slots = k_cache.shape[0] * BLOCK_SIZE
     N.check(N.load().as_rope_reshape_and_cache(
         _ptr(q), q.stride(0) if q is not None else H * D, _ptr(k), k.stride(0), _ptr(v),
@@ -214,8 +223,11 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
     _cuda(q, k_cache, v_cache, block_tables, seq_lens_k, workspace, out)
     B, H, D = q.shape
     NB, bs, Kh, D2 = k_cache.shape
-    assert bs == BLOCK_SIZE and D2 == D and _row_view_ok(q)
-    assert block_tables.dtype == torch.int32 and block_tables.stride(1) == 1
+    _require(bs == BLOCK_SIZE and D2 == D and v_cache.shape == k_cache.shape,
+             "k_cache / v_cache must be [NB, 16, Kh, D] with q's head_dim")
+    _require(_row_view_ok(q), "q must be [B, H, D] with contiguous rows")
+    _require(block_tables.dtype == torch.int32 and block_tables.stride(1) == 1,
+             "block_tables must be int32 with contiguous rows")
     max_blocks = block_tables.shape[1]
     if out is None:
         out = torch.empty(B, H * D, dtype=q.dtype, device=q.device)
@@ -253,8 +265,11 @@ def varlen_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: to
     _cuda(q, k_cache, v_cache, block_tables, cu_seqlens_q, seq_lens_k, out, workspace)
     Tq, H, D = q.shape
     NB, bs, Kh, D2 = k_cache.shape
-    assert bs == BLOCK_SIZE and D2 == D and _row_view_ok(q)
-    assert block_tables.dtype == torch.int32 and block_tables.stride(1) == 1
+    _require(bs == BLOCK_SIZE and D2 == D and v_cache.shape == k_cache.shape,
+             "k_cache / v_cache must be [NB, 16, Kh, D] with q's head_dim")
+    _require(_row_view_ok(q), "q must be [T, H, D] with contiguous rows")
+    _require(block_tables.dtype == torch.int32 and block_tables.stride(1) == 1,
+             "block_tables must be int32 with contiguous rows")
     R = seq_lens_k.shape[0]
     mb = block_tables.shape[1]
     if out is None:
@@ -287,10 +302,12 @@ def linear_small_m(x: torch.Tensor, w: torch.Tensor,
     _cuda(x, w, out)
     M, K = x.shape
     Nn = w.shape[0]
-    assert w.shape[1] == K and w.is_contiguous() and x.stride(1) == 1 and x.dtype == w.dtype
+    _require(w.shape[1] == K and w.is_contiguous() and x.stride(1) == 1 and x.dtype == w.dtype,
+             "linear_small_m: w must be a contiguous [N, K] of x's dtype, x rows contiguous")
     if out is None:
         out = torch.empty(M, Nn, dtype=x.dtype, device=x.device)
-    assert out.stride(1) == 1
+    _require(out.shape == (M, Nn) and out.stride(1) == 1 and out.dtype == x.dtype,
+             "linear_small_m: out must be [M, N] of x's dtype with contiguous rows")
     N.check(N.load().as_linear_small_m(
         _ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(w), M, Nn, K, dtype_code(x.dtype),
         _stream(x.device)), "as_linear_small_m")
@@ -310,7 +327,9 @@ def greedy_argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> t
     fixed buffer per device (so CUDA graphs keep its address), for up to 4096 rows."""
     _cuda(logits, out)
     B, V = logits.shape
-    assert logits.stride(1) == 1
+    _require(logits.stride(1) == 1, "greedy_argmax: logits rows must be contiguous")
+    _require(out is None or (out.shape == (B,) and out.dtype == torch.int64 and out.is_contiguous()),
+             "greedy_argmax: out must be a contiguous int64 [B]")
     if out is None:
         out = torch.empty(B, dtype=torch.int64, device=logits.device)
     if B > GREEDY_WS_ROWS:
@@ -351,9 +370,11 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
             out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """RMSNorm of the rows of x [rows, dim] (llama.py:39-56)."""
     _cuda(x, weight, out)
-    assert x.is_contiguous() and weight.is_contiguous()
+    _require(x.is_contiguous() and weight.is_contiguous(), "rmsnorm: x and weight must be contiguous")
     if out is None:
         out = torch.empty_like(x)
+    _require(out.shape == x.shape and out.dtype == x.dtype and out.is_contiguous(),
+             "rmsnorm: out must be a contiguous tensor like x")
     rows, dim = x.shape[0], x.shape[-1]
     N.check(N.load().as_rmsnorm(_ptr(out), _ptr(x), _ptr(weight), x.numel() // dim, dim,
                                 float(eps), dtype_code(x.dtype), _stream(x.device)), "as_rmsnorm")
@@ -364,9 +385,12 @@ def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps:
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x += delta in place (rounded to x.dtype), returns rmsnorm(x)."""
     _cuda(x, delta, weight, out)
-    assert x.is_contiguous() and delta.is_contiguous() and delta.shape == x.shape
+    _require(x.is_contiguous() and delta.is_contiguous() and delta.shape == x.shape and
+             weight.is_contiguous(), "add_rmsnorm: x, delta (same shape) and weight must be contiguous")
     if out is None:
         out = torch.empty_like(x)
+    _require(out.shape == x.shape and out.dtype == x.dtype and out.is_contiguous(),
+             "add_rmsnorm: out must be a contiguous tensor like x")
     dim = x.shape[-1]
     N.check(N.load().as_add_rmsnorm(_ptr(out), _ptr(x), _ptr(delta), _ptr(weight),
                                     x.numel() // dim, dim, float(eps), dtype_code(x.dtype),
@@ -377,11 +401,14 @@ def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps:
 def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """gate_up [rows, 2*I] -> silu(gate) * up [rows, I] (llama.py:207-211)."""
     _cuda(gate_up, out)
-    assert gate_up.is_contiguous()
+    _require(gate_up.is_contiguous() and gate_up.shape[1] % 2 == 0,
+             "silu_mul: gate_up must be a contiguous [rows, 2*I]")
     rows, two_i = gate_up.shape
     inter = two_i // 2
     if out is None:
         out = torch.empty(rows, inter, dtype=gate_up.dtype, device=gate_up.device)
+    _require(out.shape == (rows, inter) and out.dtype == gate_up.dtype and out.is_contiguous(),
+             "silu_mul: out must be a contiguous [rows, I] of gate_up's dtype")
     N.check(N.load().as_silu_mul(_ptr(out), _ptr(gate_up), rows, inter,
                                  dtype_code(gate_up.dtype), _stream(gate_up.device)),
             "as_silu_mul")
