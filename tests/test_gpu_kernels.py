@@ -579,3 +579,26 @@ def test_silu_mul_matches_reference_formula(dtype):
     out = ops.silu_mul(gu.to(DEV))
     tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
     torch.testing.assert_close(out.cpu().float(), ref.float(), **tol)
+
+
+def test_ops_reject_bad_layouts_with_value_error():
+    """Layout and dtype mistakes raise ValueError before any launch (also under -O)."""
+    x = torch.randn(4, 64, device=DEV)
+    w = torch.ones(64, device=DEV)
+    with pytest.raises(ValueError):
+        ops.rmsnorm(x.t(), w, 1e-5)                        # non-contiguous rows
+    with pytest.raises(ValueError):
+        ops.rmsnorm(x, w, 1e-5, out=torch.empty(4, 32, device=DEV))
+    with pytest.raises(ValueError):
+        ops.add_rmsnorm(x, torch.randn(4, 32, device=DEV), w, 1e-5)
+    with pytest.raises(ValueError):
+        ops.silu_mul(torch.randn(4, 63, device=DEV))       # odd width
+    with pytest.raises(ValueError):
+        ops.greedy_argmax(torch.randn(64, 4, device=DEV).t())
+    xb = torch.randn(8, 128, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.linear_small_m(xb, torch.randn(256, 128, device=DEV, dtype=torch.float16))
+    with pytest.raises(ValueError):
+        ops.linear_small_m(xb, torch.randn(256, 128, device=DEV, dtype=torch.bfloat16),
+                           out=torch.empty(8, 128, device=DEV, dtype=torch.bfloat16))
+    status_ok()
