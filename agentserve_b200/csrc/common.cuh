@@ -12,9 +12,48 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/agentserve_b200.h"
 
 namespace asb {
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (the decode step's own kernels).  A kernel launched
+// with launch_pdl() may be scheduled while the previous kernel of the stream is still
+// running; it calls pdl_wait() before touching any memory, which returns once that
+// kernel has finished and its writes are visible (immediately for a normal launch).
+// pdl_trigger() lets the next such kernel be scheduled early.  Only the launch and
+// block start-up overlap; no data is read before the wait.
+// ---------------------------------------------------------------------------
+#ifndef AS_PDL
+#define AS_PDL 1
+#endif
+__device__ __forceinline__ void pdl_wait() {
+#if AS_PDL
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void pdl_trigger() {
+#if AS_PDL
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = AS_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Device status word.  Kernels never trap: a bad block id, a bad slot or a

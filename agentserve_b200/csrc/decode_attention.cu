@@ -272,6 +272,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
   using Cfg = FastCfg<D>;
   constexpr int NS = Cfg::kStages;
   constexpr int KT = D / 16;  // k-steps of QK^T == m-tiles of O^T
+  pdl_wait();  // programmatic launch: q and the new token's K/V come from the kernel before
+  pdl_trigger();
 
   const int split = blockIdx.x;
   const int g = blockIdx.y;
@@ -639,9 +641,9 @@ int launch_fast(T* out, const T* q, int64_t q_stride, const void* k_cache, const
   auto kern = decode_fast_kernel<T, D>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   dim3 grid(max_splits, Kh, B);
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
-      mk, mv, out, q, q_stride, bt, bt_stride, seq_lens_k, H, Kh, H / Kh, num_blocks, max_blocks,
-      scale * kLog2e, bps, max_splits, os_h, os_d, ws, device_status_ptr());
+  launch_pdl(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, mk, mv, out, q, q_stride,
+             bt, bt_stride, seq_lens_k, H, Kh, H / Kh, num_blocks, max_blocks, scale * kLog2e, bps,
+             max_splits, os_h, os_d, ws, device_status_ptr());
   return check_launch("as_paged_decode_attention");
 }
 

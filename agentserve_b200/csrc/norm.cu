@@ -35,6 +35,8 @@ template <typename T, int VEC, int THREADS, int ROW_VECS, bool ADD>
 __global__ void __launch_bounds__(THREADS)
 rmsnorm_kernel(T* __restrict__ y, T* __restrict__ x, const T* __restrict__ d,
                const T* __restrict__ w, int dim, float eps) {
+  pdl_wait();  // programmatic launch: nothing is touched before the previous kernel ends
+  pdl_trigger();
   using P = Pack<T, VEC>;
   __shared__ float red[THREADS / 32];
   const int64_t row = blockIdx.x;
@@ -79,6 +81,8 @@ template <typename T, bool ADD>
 __global__ void __launch_bounds__(256)
 rmsnorm_generic_kernel(T* __restrict__ y, T* __restrict__ x, const T* __restrict__ d,
                        const T* __restrict__ w, int dim, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   T* xr = x + row * dim;
@@ -103,6 +107,8 @@ rmsnorm_generic_kernel(T* __restrict__ y, T* __restrict__ x, const T* __restrict
 template <typename T, int VEC>
 __global__ void silu_mul_kernel(T* __restrict__ y, const T* __restrict__ gu, int64_t rows,
                                 int inter) {
+  pdl_wait();
+  pdl_trigger();
   using P = Pack<T, VEC>;
   const int per_row = inter / VEC;
   const int64_t total = rows * per_row;
@@ -135,15 +141,15 @@ int launch_rmsnorm(void* y, void* x, const void* d, const void* w, int64_t rows,
                         reinterpret_cast<uintptr_t>(w) | (ADD ? reinterpret_cast<uintptr_t>(d) : 0)) &
                        15) == 0;
   if (vec_ok && dim == 256 * VEC * 1)
-    rmsnorm_kernel<T, VEC, 256, 1, ADD><<<rows, 256, 0, s>>>(yy, xx, dd, ww, dim, eps);
+    launch_pdl(rmsnorm_kernel<T, VEC, 256, 1, ADD>, dim3(unsigned(rows)), dim3(256), 0, s, yy, xx, dd, ww, dim, eps);
   else if (vec_ok && dim == 256 * VEC * 2)
-    rmsnorm_kernel<T, VEC, 256, 2, ADD><<<rows, 256, 0, s>>>(yy, xx, dd, ww, dim, eps);
+    launch_pdl(rmsnorm_kernel<T, VEC, 256, 2, ADD>, dim3(unsigned(rows)), dim3(256), 0, s, yy, xx, dd, ww, dim, eps);
   else if (vec_ok && dim == 256 * VEC * 3)
-    rmsnorm_kernel<T, VEC, 256, 3, ADD><<<rows, 256, 0, s>>>(yy, xx, dd, ww, dim, eps);
+    launch_pdl(rmsnorm_kernel<T, VEC, 256, 3, ADD>, dim3(unsigned(rows)), dim3(256), 0, s, yy, xx, dd, ww, dim, eps);
   else if (vec_ok && dim == 256 * VEC * 4)
-    rmsnorm_kernel<T, VEC, 256, 4, ADD><<<rows, 256, 0, s>>>(yy, xx, dd, ww, dim, eps);
+    launch_pdl(rmsnorm_kernel<T, VEC, 256, 4, ADD>, dim3(unsigned(rows)), dim3(256), 0, s, yy, xx, dd, ww, dim, eps);
   else
-    rmsnorm_generic_kernel<T, ADD><<<rows, 256, 0, s>>>(yy, xx, dd, ww, dim, eps);
+    launch_pdl(rmsnorm_generic_kernel<T, ADD>, dim3(unsigned(rows)), dim3(256), 0, s, yy, xx, dd, ww, dim, eps);
   return check_launch(ADD ? "as_add_rmsnorm" : "as_rmsnorm");
 }
 
@@ -171,8 +177,8 @@ int launch_silu_mul(void* y, const void* gu, int64_t rows, int inter, cudaStream
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = int64_t(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
-  silu_mul_kernel<T, VEC><<<int(blocks), 256, 0, s>>>(static_cast<T*>(y),
-                                                      static_cast<const T*>(gu), rows, inter);
+  launch_pdl(silu_mul_kernel<T, VEC>, dim3(unsigned(blocks)), dim3(256), 0, s, static_cast<T*>(y),
+             static_cast<const T*>(gu), rows, inter);
   return check_launch("as_silu_mul");
 }
 

@@ -31,6 +31,8 @@ __global__ void rope_cache_kernel(T* __restrict__ q, int64_t q_stride, const T* 
                                   T* __restrict__ k_cache, T* __restrict__ v_cache,
                                   int64_t num_slots, T* __restrict__ k_out, int32_t T_tokens,
                                   int32_t H, int32_t Kh, int32_t D, int* status) {
+  pdl_wait();  // launched programmatically: the projection that produced q/k/v may still run
+  pdl_trigger();
   using V = Vec<T, VEC>;
   const int half = D >> 1;
   const int chunks = half / VEC;
@@ -139,7 +141,7 @@ int launch_rope_cache(void* q, int64_t q_stride, const void* k, int64_t k_stride
   int64_t blocks = (total + threads - 1) / threads;
   const int64_t cap = int64_t(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
-  rope_cache_kernel<T, VEC><<<int(blocks), threads, 0, stream>>>(
+  launch_pdl(rope_cache_kernel<T, VEC>, dim3(unsigned(blocks)), dim3(threads), 0, stream,
       static_cast<T*>(q), q_stride, static_cast<const T*>(k), k_stride,
       static_cast<const T*>(v), v_stride, positions, slot_mapping, cos_sin, table_len,
       static_cast<T*>(k_cache), static_cast<T*>(v_cache), num_slots, static_cast<T*>(k_out),
