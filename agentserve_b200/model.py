@@ -438,7 +438,7 @@ class B200LlamaModel(nn.Module):
         max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
         bps = self.decode_blocks_per_split
         if (self.decode_graphs and dev.type == "cuda" and
-                list(position_offsets) == list(seq_lens)):
+                (position_offsets is seq_lens or list(position_offsets) == list(seq_lens))):
             return self._graphed_decode(allocator, last_token_ids, seq_lens, rows, max_blocks,
                                         bps), None
         host = torch.tensor([list(last_token_ids), list(seq_lens), rows, list(position_offsets)],
@@ -494,6 +494,7 @@ class _PagedStepGraph:
         self.allocator = allocator
         dev = model.device
         self.host = torch.zeros(3, B, dtype=torch.int32).pin_memory()
+        self._host_np = self.host.numpy()
         self.inputs = torch.zeros(3, B, dtype=torch.int32, device=dev)
         self.copied = torch.cuda.Event()
         self.ws = ops.new_decode_workspace(B, model.H, model.Kh, model.D, max_blocks, bps, dev)
@@ -514,13 +515,13 @@ class _PagedStepGraph:
 
     def _stage(self, tokens, seq_lens, rows) -> None:
         self.copied.synchronize()  # the previous call's copy has left the pinned buffer
-        h = self.host.numpy()
+        h = self._host_np
         h[0], h[1], h[2] = tokens, seq_lens, rows
         self.inputs.copy_(self.host, non_blocking=True)
         self.copied.record()
 
-    @torch.inference_mode()
     def run(self, tokens, seq_lens, rows) -> torch.Tensor:
+        """Called from forward_decode_paged (inference mode)."""
         self._stage(tokens, seq_lens, rows)
         if self.graph is None:
             # warm-up on a side stream (kernel attributes, cuBLAS workspaces), then
