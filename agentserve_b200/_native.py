@@ -28,6 +28,9 @@ AS_LAYOUT_DIM_MAJOR = 1
 
 AS_DECODE_NOALLOC_SCRATCH_BYTES = 8 << 20
 
+AS_KERNEL_DECODE_ATTENTION = 1
+AS_KERNEL_PREFILL_ATTENTION = 2
+
 # Every exported entry point with its C signature (restype, argtypes).
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -67,6 +70,8 @@ SIGNATURES = {
     "as_silu_mul": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P]),
     "as_block_copy": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _I64, _I32, _I32,
                                      _P]),
+    "as_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
+    "as_debug_starve_next_launch": (ctypes.c_int, [ctypes.c_int]),
 }
 
 

@@ -1,4 +1,5 @@
 // C-ABI plumbing: error strings, the per-device status word, tensor-map encoding.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -16,9 +17,15 @@ thread_local char g_last_error[512] = {0};
 __device__ int g_device_status;
 
 constexpr int kMaxDevices = 64;
-int* g_status_ptr[kMaxDevices] = {nullptr};
-int g_sm_count[kMaxDevices] = {0};
+// Per-device caches filled once under g_mu and read without it afterwards: atomics
+// (acquire / release) so a reader never sees a half-published value.
+std::atomic<int*> g_status_ptr[kMaxDevices];
+std::atomic<int> g_sm_count[kMaxDevices];
 std::mutex g_mu;
+
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
+std::atomic<int> g_starve_next{0};
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -44,25 +51,35 @@ int check_launch(const char* what) {
 int* device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (g_status_ptr[dev]) return g_status_ptr[dev];
+  int* p = g_status_ptr[dev].load(std::memory_order_acquire);
+  if (p) return p;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_status_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    g_status_ptr[dev] = static_cast<int*>(p);
+  p = g_status_ptr[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_device_status) != cudaSuccess) return nullptr;
+    p = static_cast<int*>(a);
+    g_status_ptr[dev].store(p, std::memory_order_release);
   }
-  return g_status_ptr[dev];
+  return p;
 }
 
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
-  if (!g_sm_count[dev]) {
-    int n = 0;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (!n) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    g_sm_count[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
   }
-  return g_sm_count[dev];
+  return n;
+}
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
+bool take_starve_flag(int kernel_bit) {
+  return (g_starve_next.fetch_and(~kernel_bit) & kernel_bit) != 0;
 }
 
 int dtype_size(int dtype) {
@@ -121,5 +138,18 @@ extern "C" int as_device_status(int clear, int* out_bits, as_stream_t stream) {
   if (cudaStreamSynchronize(s) != cudaSuccess)
     return asb::fail(AS_ERR_CUDA, "as_device_status: sync failed");
   if (out_bits) *out_bits = bits;
+  return AS_OK;
+}
+
+extern "C" uint64_t as_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns == 0) limit_ns = asb::kDefaultWaitLimitNs;
+  return asb::g_wait_limit_ns.exchange(limit_ns);
+}
+
+extern "C" int as_debug_starve_next_launch(int kernels) {
+  if (kernels & ~(AS_KERNEL_DECODE_ATTENTION | AS_KERNEL_PREFILL_ATTENTION))
+    return asb::fail(AS_ERR_INVALID_ARG, "as_debug_starve_next_launch: unknown kernel bits %d",
+                     kernels);
+  asb::g_starve_next.store(kernels);
   return AS_OK;
 }

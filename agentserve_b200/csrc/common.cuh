@@ -157,7 +157,10 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // Returns false (and flags the status word) if the wait ran out.  The global timer
 // is slow to read, so it is first read after 256 polls (a wait that ends sooner
 // reads it never) and then every 256 polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// `limit_ns` is the kernel's wait limit (kWaitLimitNs unless the host set another,
+// as_set_wait_limit_ns).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -165,7 +168,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
       const uint64_t now = global_timer_ns();
       if (i == 255u)
         t0 = now;
-      else if (now - t0 > kWaitLimitNs)
+      else if (now - t0 > limit_ns)
         break;
     }
   }

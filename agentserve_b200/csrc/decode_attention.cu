@@ -19,6 +19,7 @@
 // Generic path (fp32, or other head dims / group sizes): CUDA-core warps with
 //   the same online softmax, used for the fp32 parity configuration and the tiny
 //   test geometry.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -268,7 +269,8 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    const T* __restrict__ q, int64_t q_stride, const int32_t* __restrict__ bt,
                    int64_t bt_stride, const int32_t* __restrict__ seq_lens_k, int H, int Kh,
                    int group, int num_blocks, int max_blocks, float scale_log2, int bps,
-                   int max_splits, int os_h, int os_d, DecodeWorkspace ws, int* status) {
+                   int max_splits, int os_h, int os_d, DecodeWorkspace ws, int* status,
+                   uint64_t wait_limit, int starve) {
   using Cfg = FastCfg<D>;
   constexpr int NS = Cfg::kStages;
   constexpr int KT = D / 16;  // k-steps of QK^T == m-tiles of O^T
@@ -321,27 +323,35 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
     }
     s_blk[i] = id;
   }
+  // Set by any thread whose wait ran out; read by all after the barrier that ends the
+  // main loop (a static __shared__ word, outside the stage buffers TMA writes to).
+  __shared__ int s_timeout;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], Cfg::kConsumerWarps);
     }
+    s_timeout = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
 
-  bool timed_out = false;
+  int issued = 0;  // producer lane 0: stages whose loads were issued
 
   if (warp == Cfg::kConsumerWarps) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0) {
+    // starve != 0 (test hook only): issue nothing, so the consumers' waits run out.
+    if (lane == 0 && !starve) {
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
       const uint64_t policy = l2_policy_evict_first();
       for (int it = 0; it < niter; ++it) {
         const int st = it % NS;
         if (it >= NS) {
-          if (!mbar_wait(&empty_bar[st], ((it / NS) + 1) & 1, status)) break;
+          if (!mbar_wait(&empty_bar[st], ((it / NS) + 1) & 1, status, wait_limit)) {
+            s_timeout = 1;
+            break;
+          }
         }
         const int nb = min(kPerStage, blk_count - it * kPerStage);
         mbar_arrive_expect_tx(&full_bar[st], uint32_t(nb * Cfg::kSlotBytes));
@@ -357,6 +367,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         &full_bar[st], sub * 64, g, 0, blk, policy);
           }
         }
+        issued = it + 1;
       }
     }
   }
@@ -379,8 +390,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const int local = it * kPerStage + warp * Cfg::kFold;  // this warp's first block
       const int n = min(Cfg::kFold, blk_count - local);       // < 1 only in the last stage
       if (n > 0) {
-        if (!mbar_wait(&full_bar[st], (it / NS) & 1, status)) {
-          timed_out = true;
+        // warp-uniform: the fold below is full-warp mma / shuffle code
+        if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[st], (it / NS) & 1, status,
+                                                wait_limit))) {
+          s_timeout = 1;
           break;
         }
         uint32_t kb[Cfg::kFold], vb[Cfg::kFold];
@@ -403,14 +416,41 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
       l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
       l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
     }
-    if (timed_out) {
-      m_run[0] = m_run[1] = -INFINITY;
-      l_run[0] = l_run[1] = 0.f;
+  }
+
+  __syncthreads();
+  const size_t part_base = (size_t(b) * H + g * group) * max_splits + split;
+  if (s_timeout) {
+    // A wait ran out (status bit 4 is set).  Loads may still be landing in the stage
+    // buffers, so the shared-memory merge below is skipped: the producer waits (bounded)
+    // for the stages it issued that were not consumed, and this CTA contributes an
+    // empty partial (or a zero row) so the split-K counter protocol still completes
+    // and leaves the counters at zero for the next call.
+    if (warp == Cfg::kConsumerWarps && lane == 0) {
+      for (int it = max(0, issued - NS); it < issued; ++it)
+        mbar_wait(&full_bar[it % NS], (it / NS) & 1, status, wait_limit);
     }
+    for (int idx = threadIdx.x; idx < group * D; idx += blockDim.x) {
+      const int hl = idx / D;
+      const int d = idx - hl * D;
+      if (nsplit == 1) {
+        write_row<T>(out + size_t(b) * H * D + (g * group + hl) * os_h + d * os_d, 0.f, 0.f);
+      } else {
+        const size_t pi = part_base + size_t(hl) * max_splits;
+        ws.part_o[pi * D + d] = 0.f;
+        if (d == 0) {
+          ws.part_m[pi] = -INFINITY;
+          ws.part_l[pi] = 0.f;
+        }
+      }
+    }
+    if (nsplit > 1)
+      splitk_finish<T>(ws, out, b, g, H, Kh, D, group, nsplit, max_splits, os_h, os_d);
+    return;
   }
 
   // ---------------------------- merge the warps -----------------------------
-  __syncthreads();  // every TMA issued was consumed: the stage buffers are free
+  // Every load issued was consumed (no wait ran out): the stage buffers are free.
   float* red_o = reinterpret_cast<float*>(smem);                      // [4][8][D]
   float* red_m = red_o + Cfg::kConsumerWarps * kMaxGroup * D;          // [4][8]
   float* red_l = red_m + Cfg::kConsumerWarps * kMaxGroup;              // [4][8]
@@ -419,10 +459,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
     for (int mt = 0; mt < KT; ++mt) {
       const int d0 = 16 * mt + gq;
-      ow[(2 * tq) * D + d0] = timed_out ? 0.f : o_acc[mt][0];
-      ow[(2 * tq + 1) * D + d0] = timed_out ? 0.f : o_acc[mt][1];
-      ow[(2 * tq) * D + d0 + 8] = timed_out ? 0.f : o_acc[mt][2];
-      ow[(2 * tq + 1) * D + d0 + 8] = timed_out ? 0.f : o_acc[mt][3];
+      ow[(2 * tq) * D + d0] = o_acc[mt][0];
+      ow[(2 * tq + 1) * D + d0] = o_acc[mt][1];
+      ow[(2 * tq) * D + d0 + 8] = o_acc[mt][2];
+      ow[(2 * tq + 1) * D + d0 + 8] = o_acc[mt][3];
     }
     if (gq == 0) {
       red_m[warp * kMaxGroup + 2 * tq] = m_run[0];
@@ -433,7 +473,6 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
   }
   __syncthreads();
 
-  const size_t part_base = (size_t(b) * H + g * group) * max_splits + split;
   for (int idx = threadIdx.x; idx < group * D; idx += blockDim.x) {
     const int hl = idx / D;
     const int d = idx - hl * D;
@@ -643,7 +682,8 @@ int launch_fast(T* out, const T* q, int64_t q_stride, const void* k_cache, const
   dim3 grid(max_splits, Kh, B);
   launch_pdl(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, mk, mv, out, q, q_stride,
              bt, bt_stride, seq_lens_k, H, Kh, H / Kh, num_blocks, max_blocks, scale * kLog2e, bps,
-             max_splits, os_h, os_d, ws, device_status_ptr());
+             max_splits, os_h, os_d, ws, device_status_ptr(), wait_limit_ns(),
+             take_starve_flag(AS_KERNEL_DECODE_ATTENTION) ? 1 : 0);
   return check_launch("as_paged_decode_attention");
 }
 
@@ -704,6 +744,36 @@ extern "C" size_t as_paged_decode_workspace_size(int32_t num_seqs, int32_t num_h
   return workspace_bytes(num_seqs, num_heads, num_heads, head_dim, max_splits);
 }
 
+namespace {
+// Argument checks shared by both decode entry points (nothing here touches the GPU).
+// Returns AS_OK when the call may proceed; num_seqs == 0 passes (nothing to do).
+int check_decode_args(const char* who, const void* out, const void* q, int64_t q_stride,
+                      const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                      int64_t bt_stride, const int32_t* seq_lens_k, int32_t num_seqs,
+                      int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                      int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                      int32_t blocks_per_split, int32_t out_layout, int32_t dtype) {
+  if (!dtype_size(dtype)) return fail(AS_ERR_INVALID_ARG, "%s: unknown dtype", who);
+  if (block_size != kBlockSize)
+    return fail(AS_ERR_UNSUPPORTED, "%s: block_size must be 16 (got %d)", who, block_size);
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
+      head_dim <= 0 || head_dim > 256 || num_blocks <= 0 || max_blocks <= 0 ||
+      bt_stride < max_blocks || blocks_per_split < 0)
+    return fail(AS_ERR_INVALID_ARG, "%s: bad sizes (B=%d H=%d Kh=%d D=%d NB=%d maxb=%d bps=%d)",
+                who, num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, max_blocks,
+                blocks_per_split);
+  if (out_layout != AS_LAYOUT_HEAD_MAJOR && out_layout != AS_LAYOUT_DIM_MAJOR)
+    return fail(AS_ERR_INVALID_ARG, "%s: unknown out_layout %d", who, out_layout);
+  if (num_seqs == 0) return AS_OK;
+  if (num_seqs > 65535) return fail(AS_ERR_INVALID_ARG, "%s: B > 65535", who);
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !seq_lens_k)
+    return fail(AS_ERR_INVALID_ARG, "%s: null pointer", who);
+  if (q_stride < int64_t(num_heads) * head_dim)
+    return fail(AS_ERR_INVALID_ARG, "%s: q_stride < H*D", who);
+  return AS_OK;
+}
+}  // namespace
+
 extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_stride,
                                          const void* k_cache, const void* v_cache,
                                          const int32_t* block_tables, int64_t bt_stride,
@@ -714,23 +784,12 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
                                          int32_t blocks_per_split, void* workspace,
                                          size_t workspace_bytes_given, int32_t out_layout,
                                          int32_t dtype, as_stream_t stream) {
-  if (!dtype_size(dtype)) return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: unknown dtype");
-  if (block_size != kBlockSize)
-    return fail(AS_ERR_UNSUPPORTED, "as_paged_decode_attention: block_size must be 16 (got %d)",
-                block_size);
-  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads ||
-      head_dim <= 0 || head_dim > 256 || num_blocks <= 0 || max_blocks <= 0 ||
-      bt_stride < max_blocks || blocks_per_split < 0)
-    return fail(AS_ERR_INVALID_ARG,
-                "as_paged_decode_attention: bad sizes (B=%d H=%d Kh=%d D=%d NB=%d maxb=%d bps=%d)",
-                num_seqs, num_heads, num_kv_heads, head_dim, num_blocks, max_blocks,
-                blocks_per_split);
+  const int rc0 = check_decode_args("as_paged_decode_attention", out, q, q_stride, k_cache,
+                                    v_cache, block_tables, bt_stride, seq_lens_k, num_seqs,
+                                    num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                                    max_blocks, blocks_per_split, out_layout, dtype);
+  if (rc0 != AS_OK) return rc0;
   if (num_seqs == 0) return AS_OK;
-  if (num_seqs > 65535) return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: B > 65535");
-  if (!out || !q || !k_cache || !v_cache || !block_tables || !seq_lens_k)
-    return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: null pointer");
-  if (q_stride < int64_t(num_heads) * head_dim)
-    return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: q_stride < H*D");
   const int group = num_heads / num_kv_heads;
   const bool fast = fast_path_ok(dtype, head_dim, group, q, q_stride, k_cache, v_cache);
   if (blocks_per_split == 0)
@@ -739,8 +798,6 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
   if (fast && blocks_per_split > FastCfg<64>::kMaxBlocksPerSplit)
     return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: blocks_per_split > %d",
                 FastCfg<64>::kMaxBlocksPerSplit);
-  if (out_layout != AS_LAYOUT_HEAD_MAJOR && out_layout != AS_LAYOUT_DIM_MAJOR)
-    return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: unknown out_layout %d", out_layout);
   DecodeWorkspace ws{nullptr, nullptr, nullptr, nullptr};
   if (max_splits > 1) {
     const size_t need = workspace_bytes(num_seqs, num_heads, num_heads, head_dim, max_splits);
@@ -751,8 +808,6 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
       return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: workspace must be 256-byte aligned");
     ws = carve_workspace(workspace, num_seqs, num_heads, num_heads, head_dim, max_splits);
   }
-  if (out_layout != AS_LAYOUT_HEAD_MAJOR && out_layout != AS_LAYOUT_DIM_MAJOR)
-    return fail(AS_ERR_INVALID_ARG, "as_paged_decode_attention: unknown out_layout %d", out_layout);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int B = num_seqs, H = num_heads, Kh = num_kv_heads, D = head_dim;
   const int os_h = out_layout == AS_LAYOUT_HEAD_MAJOR ? D : 1;
@@ -813,7 +868,9 @@ static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[AS_DECODE_NOAL
 
 namespace {
 constexpr int kNoallocMaxDevices = 64;
-void* g_noalloc_scratch_ptr[kNoallocMaxDevices] = {nullptr};
+// Filled once per device under g_noalloc_mu and read without the lock afterwards, so
+// the slots are atomics (acquire load, release store).
+std::atomic<void*> g_noalloc_scratch_ptr[kNoallocMaxDevices];
 std::mutex g_noalloc_mu;
 
 // Device address of the scratch array on the current device.  The first call on a
@@ -825,19 +882,20 @@ int noalloc_scratch_on_current_device(void** out) {
   if (e != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices)
     return fail(AS_ERR_CUDA, "as_paged_decode_attention_noalloc: no current device (%s)",
                 cudaGetErrorString(e));
-  if (!g_noalloc_scratch_ptr[dev]) {
+  void* p = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_scratch_ptr[dev]) {
-      void* p = nullptr;
+    p = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!p) {
       e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
       if (e != cudaSuccess || !p)
         return fail(AS_ERR_CUDA,
                     "as_paged_decode_attention_noalloc: cudaGetSymbolAddress failed: %s",
                     cudaGetErrorString(e));
-      g_noalloc_scratch_ptr[dev] = p;
+      g_noalloc_scratch_ptr[dev].store(p, std::memory_order_release);
     }
   }
-  *out = g_noalloc_scratch_ptr[dev];
+  *out = p;
   return AS_OK;
 }
 }  // namespace
@@ -848,12 +906,14 @@ extern "C" int as_paged_decode_attention_noalloc(
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
     int32_t num_blocks, int32_t max_blocks, float scale, int32_t blocks_per_split,
     int32_t out_layout, int32_t dtype, as_stream_t stream) {
-  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || max_blocks <= 0 ||
-      blocks_per_split < 0)
-    return as_paged_decode_attention(out, q, q_stride, k_cache, v_cache, block_tables,
-                                     bt_stride, seq_lens_k, num_seqs, num_heads, num_kv_heads,
-                                     head_dim, block_size, num_blocks, max_blocks, scale,
-                                     blocks_per_split, nullptr, 0, out_layout, dtype, stream);
+  // Bad arguments are reported as such (AS_ERR_INVALID_ARG / AS_ERR_UNSUPPORTED) before
+  // the scratch is looked at.
+  const int rc0 = check_decode_args("as_paged_decode_attention_noalloc", out, q, q_stride,
+                                    k_cache, v_cache, block_tables, bt_stride, seq_lens_k,
+                                    num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                                    num_blocks, max_blocks, blocks_per_split, out_layout, dtype);
+  if (rc0 != AS_OK) return rc0;
+  if (num_seqs == 0) return AS_OK;
   // blocks_per_split == 0 (split chosen by the library) may use scratch
   const bool uses_scratch =
       blocks_per_split == 0 || (max_blocks + blocks_per_split - 1) / blocks_per_split > 1;

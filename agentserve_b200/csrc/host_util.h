@@ -28,4 +28,12 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank
 // Number of SMs on the current device (cached per device).
 int sm_count();
 
+// Limit of every bounded mbarrier wait in the kernels launched from now on
+// (as_set_wait_limit_ns; 2 s unless changed).
+uint64_t wait_limit_ns();
+
+// Test hook of as_debug_starve_next_launch: true (once) if the next launch of the
+// attention kernel `kernel_bit` (AS_KERNEL_*) must issue no loads.
+bool take_starve_flag(int kernel_bit);
+
 }  // namespace asb

@@ -150,7 +150,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const int32_t* __restrict__ cu_seqlens_q,
                     const int32_t* __restrict__ seq_lens_k, int H, int group, int num_blocks,
                     int max_blocks, float scale_log2, int run8_ok, int n_split,
-                    float* __restrict__ part_o, float2* __restrict__ part_ml, int* status) {
+                    float* __restrict__ part_o, float2* __restrict__ part_ml, int* status,
+                    uint64_t wait_limit, int starve) {
   using Cfg = PairCfg<HD>;
   constexpr int D = Cfg::D;
   constexpr int NS = Cfg::kStages;
@@ -232,8 +233,12 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t sQ = smem_u32(smem + Cfg::kOffQ);
   const uint32_t sKV = smem_u32(smem + Cfg::kOffKV);
 
+  int kv_issued = 0;  // producer warp: K/V tiles whose loads were issued
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // (starve != 0 is the test hook of as_debug_starve_next_launch: no loads at all,
+    // so every wait on them runs out)
+    if (!starve) {
     const int filler = (nblk_seq > 0) ? bt[int64_t(r) * bt_stride] : 0;
     const int fill_ok = (filler >= 0 && filler < num_blocks) ? filler : 0;
     if (lane == 0) {
@@ -266,7 +271,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     for (int j = 0; j < n_load; ++j) {  // local tile index; global tile j0 + j
       if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
       const int st = j % NS;
-      const bool ready = j < NS || mbar_wait(&bars->kv_empty[st], ((j / NS) + 1) & 1, status);
+      const bool ready = j < NS || mbar_wait(&bars->kv_empty[st], ((j / NS) + 1) & 1, status, wait_limit);
       if (!__all_sync(0xffffffffu, ready)) {
         *abort_flag = 1;
         break;
@@ -297,7 +302,9 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       &bars->kv_full[st], sb * 64, g, 0, id, pol_kv);
         }
       }
+      kv_issued = j + 1;
       __syncwarp();
+    }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -322,7 +329,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
           tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kSubBytes, 1024),
                          kIdescO, (acc || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->q_full, 0, status);
+      bool ok = mbar_wait(&bars->q_full, 0, status, wait_limit);
       int js[2] = {0, 0};  // next S tile per query tile
       int jp[2] = {0, 0};  // next PV tile per query tile
       uint64_t t_idle = 0;  // start of the current stretch without progress
@@ -361,7 +368,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
           const uint64_t now = global_timer_ns();
           if (spin == 256u) {
             t_idle = now;
-          } else if (now - t_idle > kWaitLimitNs) {
+          } else if (now - t_idle > wait_limit) {
             flag_status(status, kStatusWaitTimeout);
             ok = false;
           }
@@ -369,7 +376,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       }
       if (!ok) *abort_flag = 1;
       tc::commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, status);
+      mbar_wait(&bars->drain, 0, status, wait_limit);
     }
     __syncwarp();
   } else {
@@ -391,7 +398,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {  // local tile index; global tile j0 + j
-      const bool go = !aborted(abort_flag) && mbar_wait(&bars->s_full[i], j & 1, status);
+      const bool go = !aborted(abort_flag) && mbar_wait(&bars->s_full[i], j & 1, status, wait_limit);
       if (!__all_sync(0xffffffffu, go)) {
         ok = false;
         break;
@@ -449,7 +456,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const bool wait_turn = AS_PREFILL_PINGPONG && (i == 0 ? (j >= 1 && j - 1 < cnt1) : (j < cnt0));
       if (wait_turn) {
         const uint32_t par = (i == 0 ? (j - 1) : j) & 1;
-        if (!__all_sync(0xffffffffu, !aborted(abort_flag) && mbar_wait(&bars->turn[i][quad], par, status))) {
+        if (!__all_sync(0xffffffffu, !aborted(abort_flag) && mbar_wait(&bars->turn[i][quad], par, status, wait_limit))) {
           ok = false;
           break;
         }
@@ -485,7 +492,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
       }
       if (j > 0) {  // PV(j-1) still reads P and accumulates into O
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (j - 1) & 1, status))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (j - 1) & 1, status, wait_limit))) {
           ok = false;
           break;
         }
@@ -512,7 +519,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
     if (!ok) *abort_flag = 1;
     const bool done = ok && nkv > 0 &&
-                      __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (nkv - 1) & 1, status));
+                      __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (nkv - 1) & 1, status, wait_limit));
     if (n_split > 1) {
       // split-KV partial: unnormalised O row, (m, l); merged by prefill_merge_kernel
       const int64_t rec = ((int64_t(r) * gridDim.y + g) * npairs + pair) * n_split + split;
@@ -566,6 +573,13 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (warp == 0 && lane == 0 && !starve && aborted(abort_flag)) {
+    // A wait ran out somewhere: let the copies this CTA started land (bounded) before
+    // its shared memory is released.  A stage already consumed completed long ago.
+    mbar_wait(&bars->q_full, 0, status, wait_limit);
+    for (int j = max(0, kv_issued - NS); j < kv_issued; ++j)
+      mbar_wait(&bars->kv_full[j % NS], (j / NS) & 1, status, wait_limit);
   }
 }
 
@@ -682,7 +696,7 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
       mq, mk, mv, mk8, mv8, static_cast<T*>(out), bt, bt_stride, cu, lk, H, group, num_blocks,
       max_blocks, scale * kLog2e, num_blocks >= 8 ? 1 : 0, n_split, part_o, part_ml,
-      device_status_ptr());
+      device_status_ptr(), wait_limit_ns(), take_starve_flag(AS_KERNEL_PREFILL_ATTENTION) ? 1 : 0);
   int rc = check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
   if (rc || n_split == 1) return rc;
   prefill_merge_kernel<T, HD><<<dim3(npairs, Kh, R), 256, 0, stream>>>(

@@ -78,6 +78,23 @@ AS_API const char* as_last_error(void);
  * 8 RoPE position outside the table, 16 sequence longer than its block-table row. */
 AS_API int as_device_status(int clear, int* out_bits, as_stream_t stream);
 
+/* Failure detection (no counterpart in the reference, which has no device code).
+ * Every mbarrier wait in the attention kernels gives up after a time limit, sets
+ * status bit 4, lets the copies it started land (again bounded), frees its tensor
+ * memory and returns, so a stuck pipeline costs one failed call, never a hung GPU.
+ * as_set_wait_limit_ns sets that limit for kernels launched from now on (0 = the
+ * default of 2 s) and returns the previous one.  Launches captured in a CUDA graph
+ * keep the limit they were captured with. */
+AS_API uint64_t as_set_wait_limit_ns(uint64_t limit_ns);
+
+/* Test hook for that path: the next launch of each kernel named in `kernels`
+ * (AS_KERNEL_* bits) issues none of its loads, so its waits run out, and the call
+ * must come back with status bit 4 set and the next call must be correct again.
+ * Each call replaces the pending set (0 clears it). */
+#define AS_KERNEL_DECODE_ATTENTION 1  /* as_paged_decode_attention, bf16/fp16 fast path */
+#define AS_KERNEL_PREFILL_ATTENTION 2 /* as_varlen_prefill_attention*, tcgen05 path */
+AS_API int as_debug_starve_next_launch(int kernels);
+
 /* ------------------------------------------------------------------------- */
 /* (1) Ragged-batch packing                                                  */
 /* ------------------------------------------------------------------------- */

@@ -116,3 +116,35 @@ def test_new_entry_points_host_checks(lib):
     rc = lib.as_greedy_argmax(None, None, 50, 4, 100, N.AS_DTYPE_BF16, None, 0, None)
     assert rc == N.AS_ERR_INVALID_ARG  # row stride < vocab
     assert lib.as_greedy_argmax(None, None, 100, 0, 100, N.AS_DTYPE_BF16, None, 0, None) == N.AS_OK
+
+
+def test_noalloc_reports_bad_arguments_as_such(lib):
+    """The allocation-free decode entry point checks its arguments before it looks at
+    its static scratch, so a bad call gets the real cause (no GPU work is done)."""
+    for H, Kh, D in ((30, 8, 64), (32, 8, 0)):
+        rc = lib.as_paged_decode_attention_noalloc(None, None, 0, None, None, None, 64, None,
+                                                   4, H, Kh, D, 16, 100, 64, 0.125, 0,
+                                                   N.AS_LAYOUT_HEAD_MAJOR, N.AS_DTYPE_BF16,
+                                                   None)
+        assert rc == N.AS_ERR_INVALID_ARG
+        assert "bad sizes" in N.last_error()
+    rc = lib.as_paged_decode_attention_noalloc(None, None, 0, None, None, None, 64, None, 4, 32,
+                                               8, 64, 8, 100, 64, 0.125, 0,
+                                               N.AS_LAYOUT_HEAD_MAJOR, N.AS_DTYPE_BF16, None)
+    assert rc == N.AS_ERR_UNSUPPORTED
+    rc = lib.as_paged_decode_attention_noalloc(None, None, 0, None, None, None, 64, None, 4, 32,
+                                               8, 64, 16, 100, 64, 0.125, 0, 7, N.AS_DTYPE_BF16,
+                                               None)
+    assert rc == N.AS_ERR_INVALID_ARG and "out_layout" in N.last_error()
+    rc = lib.as_paged_decode_attention_noalloc(None, None, 2048, None, None, None, 64, None, 4,
+                                               32, 8, 64, 16, 100, 64, 0.125, 0,
+                                               N.AS_LAYOUT_HEAD_MAJOR, N.AS_DTYPE_BF16, None)
+    assert rc == N.AS_ERR_INVALID_ARG and "null pointer" in N.last_error()
+
+
+def test_wait_limit_and_starve_hook_are_host_settings(lib):
+    prev = lib.as_set_wait_limit_ns(1_000_000)
+    assert prev == 2_000_000_000
+    assert lib.as_set_wait_limit_ns(0) == 1_000_000  # 0 restores the default
+    assert lib.as_set_wait_limit_ns(0) == 2_000_000_000
+    assert lib.as_debug_starve_next_launch(8) == N.AS_ERR_INVALID_ARG

@@ -5,8 +5,11 @@ static array inside the library instead of a caller workspace.
 
 Checked here through the C ABI (ctypes): two calls in a row, with different batch
 sizes so the second reuses the array the first left behind, each against the
-regular entry point on the same inputs; and a call whose scratch need exceeds the
-static array is refused before any GPU work.  The file is named to run last.
+regular entry point on the same inputs and against the oracle (the reference's
+gather -> pad -> SDPA restated on the CPU in fp32); with a fixed split and with the
+split left to the library (blocks_per_split 0), at head_dim 64 and 128; and a call
+whose scratch need exceeds the static array is refused before any GPU work.  The
+file is named to run last.
 """
 
 import ctypes
@@ -17,6 +20,7 @@ import torch
 
 from agentserve_b200 import _native as N
 from agentserve_b200 import ops
+from oracle import attention as OA
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -37,6 +41,15 @@ def _case(lens, H, Kh, D, dtype, seed):
     vp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype).to(DEV)
     q = torch.randn(len(lens), H, D, generator=g).to(dtype).to(DEV)
     return q, kp, vp, bt.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV)
+
+
+def _oracle(q, kp, vp, bt, lens, layout):
+    tables = [bt[i, :(L + 15) // 16].tolist() for i, L in enumerate(lens)]
+    o = OA.decode_attention_from_pool(q.cpu().float(), kp.cpu().float(), vp.cpu().float(),
+                                      tables, lens)
+    if layout == N.AS_LAYOUT_DIM_MAJOR:
+        return OA.flatten_decode_output(o)
+    return o.reshape(len(lens), -1)
 
 
 def _noalloc(q, kp, vp, bt, lk, bps, layout):
@@ -60,18 +73,29 @@ def _regular(q, kp, vp, bt, lk, bps, layout):
                                       out_layout=layout)
 
 
-@pytest.mark.parametrize("dtype,atol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-5)])
-def test_noalloc_matches_regular_entry_point_two_calls(dtype, atol):
-    H, Kh, D = 32, 8, 64
-    calls = [([17, 900, 3, 2048, 160], 8, N.AS_LAYOUT_HEAD_MAJOR),
-             ([4096, 1, 700, 33, 1500, 2600, 64, 999, 16, 3000, 250, 1800], 8,
+# (dtype, head_dim, blocks_per_split, tolerance against the fp32 oracle and between the
+# two entry points): 1e-5 in fp32, 2e-2 absolute in bf16 / fp16.  blocks_per_split 0
+# lets the library choose the split inside the call (the scratch is sized for the
+# finest split it may choose).
+CASES = [(torch.bfloat16, 64, 8, 2e-2), (torch.float32, 64, 8, 1e-5),
+         (torch.bfloat16, 64, 0, 2e-2), (torch.float16, 128, 0, 2e-2),
+         (torch.bfloat16, 128, 16, 2e-2)]
+
+
+@pytest.mark.parametrize("dtype,D,bps,atol", CASES)
+def test_noalloc_matches_regular_entry_point_and_oracle_two_calls(dtype, D, bps, atol):
+    H, Kh = 32, 8
+    calls = [([17, 900, 3, 2048, 160], N.AS_LAYOUT_HEAD_MAJOR),
+             ([4096, 1, 700, 33, 1500, 2600, 64, 999, 16, 3000, 250, 1800],
               N.AS_LAYOUT_DIM_MAJOR)]
-    for i, (lens, bps, layout) in enumerate(calls):
-        q, kp, vp, bt, lk = _case(lens, H, Kh, D, dtype, seed=100 + i)
+    for i, (lens, layout) in enumerate(calls):
+        q, kp, vp, bt, lk = _case(lens, H, Kh, D, dtype, seed=100 + i + D)
         got = _noalloc(q, kp, vp, bt, lk, bps, layout)
         want = _regular(q, kp, vp, bt, lk, bps, layout)
         torch.cuda.synchronize()
         torch.testing.assert_close(got.float(), want.float(), rtol=0, atol=atol)
+        ref = _oracle(q, kp, vp, bt, lens, layout)
+        torch.testing.assert_close(got.float().cpu(), ref, rtol=0, atol=atol)
     assert ops.device_status(clear=True) == 0
 
 
