@@ -162,6 +162,26 @@ class DeviceBlockAllocator:
     def ref_count(self, block_id: int) -> int:
         return self._ref[block_id]
 
+    def num_free_rows(self) -> int:
+        return len(self._free_rows)
+
+    def can_admit(self, num_blocks: int, shared: int = 0) -> bool:
+        """True if a new request holding `shared` shared blocks plus `num_blocks` blocks
+        of its own fits: free blocks, a free table row and the row's width."""
+        return (len(self._free) >= num_blocks and bool(self._free_rows)
+                and shared + num_blocks <= self.max_blocks_per_seq)
+
+    _PAD_ID = "\x00pad"
+
+    def scratch_row(self) -> int:
+        """Table row of a one-block scratch sequence (taken once, never freed): padding
+        rows of a bucketed decode batch write their dummy token there."""
+        row = self._rows.get(self._PAD_ID)
+        if row is None:
+            self.allocate(self._PAD_ID, 1)
+            row = self._rows[self._PAD_ID]
+        return row
+
     def blocks_for(self, request_id: str) -> List[int]:
         return list(self._request_blocks.get(request_id, []))
 

@@ -338,6 +338,16 @@ class B200LlamaModel(nn.Module):
         last = pk.cu_seqlens_q[1:].long() - 1
         return self._logits(h.index_select(0, last))
 
+    def prefill_paged_greedy(self, token_ids: Sequence[Sequence[int]],
+                             num_cached: Sequence[int], allocator,
+                             request_ids: Sequence[str]) -> List[int]:
+        """forward_prefill_paged followed by greedy sampling of each request's last
+        position (engine.py:321), returning the first output tokens with one copy."""
+        if len(token_ids) == 0:
+            return []
+        return greedy(self.forward_prefill_paged(token_ids, num_cached, allocator,
+                                                 request_ids)).tolist()
+
     # ------------------------------------------------------------------ decode (lists)
     @torch.inference_mode()
     def forward_decode_batch(self, last_token_ids: List[int], kv_caches: list,
@@ -453,25 +463,60 @@ class B200LlamaModel(nn.Module):
 
 
     def _graphed_decode(self, allocator, tokens, seq_lens, rows, max_blocks: int,
-                        bps: int) -> torch.Tensor:
+                        bps: int, sample: bool = False) -> torch.Tensor:
         """forward_decode_paged through a cached CUDA graph.  Graphs are keyed by the
         allocator, the batch size and max_blocks rounded up to a power of two (capped by
         the allocator's table width); the split-K decomposition follows that bucket.
-        Least recently used graphs beyond max_decode_graphs are released."""
+        sample=True captures greedy sampling too and returns next tokens instead of
+        logits.  Least recently used graphs beyond max_decode_graphs are released."""
         B = len(tokens)
         cap = allocator.block_tables.shape[1]
         mb = min(cap, 1 << max(0, (max_blocks - 1).bit_length()))
-        key = (id(allocator), B, mb, bps)
+        key = (id(allocator), B, mb, bps, sample)
         g = self._graphs.get(key)
         if g is None or g.allocator is not allocator:
             if self._graph_pool is None:
                 self._graph_pool = torch.cuda.graph_pool_handle()
-            g = _PagedStepGraph(self, allocator, B, mb, bps, self._graph_pool)
+            g = _PagedStepGraph(self, allocator, B, mb, bps, self._graph_pool, sample)
             self._graphs[key] = g
             while len(self._graphs) > self.max_decode_graphs:
                 self._graphs.popitem(last=False)
         self._graphs.move_to_end(key)
         return g.run(tokens, seq_lens, rows)
+
+    @torch.inference_mode()
+    def decode_paged_greedy(self, last_token_ids: List[int], seq_lens: List[int], allocator,
+                            request_ids: List[str]) -> List[int]:
+        """One greedy decode step of the batch (forward_decode_paged with position =
+        seq_len, then sampling.py:46-58's greedy branch) returning the next token ids
+        with one device-to-host copy.  The step replays a CUDA graph captured for the
+        batch size rounded up to a bucket (1, 2, 4, 8, then multiples of 8 up to 64 and
+        of 32 above); the padding rows decode a dummy token in the allocator's scratch
+        row and are dropped, so a batch that shrinks or grows by a few requests reuses
+        the same graph."""
+        if not isinstance(allocator, DeviceBlockAllocator):
+            raise TypeError("decode_paged_greedy needs an agentserve_b200.DeviceBlockAllocator")
+        self.fuse_projections_()
+        B = len(last_token_ids)
+        if B == 0:
+            return []
+        rows = allocator.rows_for(request_ids)
+        max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
+        Bp = _batch_bucket(B)
+        if Bp > B:
+            pad = allocator.scratch_row()
+            last_token_ids = list(last_token_ids) + [0] * (Bp - B)
+            seq_lens = list(seq_lens) + [0] * (Bp - B)
+            rows = rows + [pad] * (Bp - B)
+        if not (self.decode_graphs and self.device.type == "cuda"):
+            host = torch.tensor([list(last_token_ids), list(seq_lens), rows], dtype=torch.int64)
+            d = host.to(self.device)
+            logits = self._decode_core(d[0], d[1].to(torch.int32), d[2].to(torch.int32),
+                                       allocator, max_blocks, self.decode_blocks_per_split)
+            return greedy(logits)[:B].tolist()
+        out = self._graphed_decode(allocator, last_token_ids, seq_lens, rows, max_blocks,
+                                   self.decode_blocks_per_split, sample=True)
+        return out[:B].tolist()
 
     def release_decode_graphs(self) -> None:
         """Drop every cached decode graph now (e.g. before destroying a process group
@@ -484,14 +529,25 @@ class B200LlamaModel(nn.Module):
         self._graph_pool = None
 
 
+def _batch_bucket(B: int) -> int:
+    """Decode batch sizes that share a captured graph: 1, 2, 4, 8, multiples of 8 up to
+    64, multiples of 32 above."""
+    if B <= 8:
+        return 1 << max(0, (B - 1).bit_length())
+    if B <= 64:
+        return (B + 7) // 8 * 8
+    return (B + 31) // 32 * 32
+
+
 class _PagedStepGraph:
     """One captured forward_decode_paged step (logits only) for a fixed batch size and
     block bucket.  Inputs travel in one pinned int32 [3, B] buffer (tokens, seq_lens,
     table rows) with one host-to-device copy per call."""
 
     def __init__(self, model: "B200LlamaModel", allocator: DeviceBlockAllocator, B: int,
-                 max_blocks: int, bps: int, pool):
+                 max_blocks: int, bps: int, pool, sample: bool = False):
         self.allocator = allocator
+        self.sample = sample
         dev = model.device
         self.host = torch.zeros(3, B, dtype=torch.int32).pin_memory()
         self._host_np = self.host.numpy()
@@ -504,8 +560,9 @@ class _PagedStepGraph:
         self.logits: Optional[torch.Tensor] = None
 
     def _body(self) -> torch.Tensor:
-        return self.model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
-                                       self.allocator, self.max_blocks, self.bps, ws=self.ws)
+        logits = self.model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
+                                         self.allocator, self.max_blocks, self.bps, ws=self.ws)
+        return greedy(logits) if self.sample else logits
 
     def release(self) -> None:
         if self.graph is not None:
