@@ -8,11 +8,21 @@ N > 1 is launched by torchrun: one replica per GPU (request-partitioned, weak
 scaling, no collective on the data path; a MAX all-reduce of the timings only).
 
 One JSON line on rank 0:
-  value        tokens/s of K graph-replayed decode steps, inputs resident in HBM;
-  e2e          tokens/s through the reference-facing call
-               model.forward_decode_paged(host lists ...) + greedy + device->host read;
-  roofline     the paged decode attention kernel, timed alone with CUDA events;
-  cpu_baseline the oracle port of the reference's forward_decode_paged on host cores.
+  value         tokens/s of K graph-replayed decode steps, inputs resident in HBM;
+  e2e           tokens/s through the reference-facing call
+                model.forward_decode_paged(host lists ...) + greedy + device->host read;
+  roofline      the paged decode attention kernel, timed alone with CUDA events;
+  per_rank      each rank's step time and host-core affinity;
+  strong        (N > 1) the same 64 sequences split over the N GPUs;
+  config5       the 8B geometry at N GPUs: request-partitioned replicas, and (N > 1)
+                KV-head tensor parallelism with one NCCL all-reduce per layer;
+  prefill       the varlen prefill kernel alone on the prefix-cache workload's shape;
+  config1       (N = 1) the single decode-attention op of the reference's CPU case,
+                on the host (mean of 50) and on the GPU at batch 8 / 64 / 256;
+  engine        (N = 1) the mixed-request and prefix-cache-session workloads through
+                B200Engine;
+  cpu_baseline  (N = 1) the oracle port of the reference's forward_decode_paged on the
+                host cores, on the same 64 sequences.
 """
 
 from __future__ import annotations
@@ -42,7 +52,7 @@ WORKLOADS = {
            "(request-partitioned replicas; 8 GPUs x 32 = the 256-sequence configuration), "
            "contexts U{{{lo}..{hi}}}, 16-token blocks, greedy"),
 }
-MODEL_DEFAULTS = {"1b": dict(batch=64, ctx_min=128, ctx_max=4096, layers=16, cpu_sample_seqs=8),
+MODEL_DEFAULTS = {"1b": dict(batch=64, ctx_min=128, ctx_max=4096, layers=16, cpu_sample_seqs=64),
                   "8b": dict(batch=32, ctx_min=1024, ctx_max=32768, layers=32, cpu_sample_seqs=2)}
 
 
@@ -58,9 +68,17 @@ def parse():
     ap.add_argument("--ctx-max", type=int, default=None)
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-sample-seqs", type=int, default=None)
-    ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    ap.add_argument("--cpu-sample-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-config1", action="store_true")
+    ap.add_argument("--no-config5", action="store_true")
+    ap.add_argument("--no-strong", action="store_true")
+    ap.add_argument("--no-engine", action="store_true",
+                    help="skip the engine workloads (mixed requests, prefix-cache sessions)")
+    ap.add_argument("--engine-sessions", type=int, default=256)
+    ap.add_argument("--engine-turns", type=int, default=4)
+    ap.add_argument("--config5-steps", type=int, default=20)
     ap.add_argument("--blocks-per-split", type=int, default=0)
     ap.add_argument("--tp", action="store_true",
                     help="KV-head tensor parallelism over all ranks instead of replicas")
@@ -77,14 +95,20 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+def config_8b(layers: int = 32):
+    from agentserve_b200.config import ModelConfig
+    return ModelConfig(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=layers,
+                       vocab_size=128256, max_seq_len=33024 + 1024, rope_theta=500000.0,
+                       intermediate_size=14336)
+
+
 def model_config(args):
     from agentserve_b200.config import ModelConfig
     if args.model == "8b":
-        return ModelConfig(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=args.layers,
-                           vocab_size=128256, max_seq_len=33024 + 1024, rope_theta=500000.0,
-                           intermediate_size=14336)
+        return config_8b(args.layers)
+    # the RoPE table covers the prefix-cache workload's longest prompts (~20K tokens)
     return ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=args.layers,
-                       vocab_size=128256, max_seq_len=8192, rope_theta=500000.0,
+                       vocab_size=128256, max_seq_len=24576, rope_theta=500000.0,
                        intermediate_size=8192)
 
 
@@ -95,6 +119,27 @@ def workload(args) -> str:
 def context_lengths(batch, lo, hi, seed):
     g = torch.Generator().manual_seed(seed)
     return torch.randint(lo, hi + 1, (batch,), generator=g).tolist()
+
+
+def line_config(args, world: int, tp: int) -> dict:
+    """The `config` object of both arms' JSON lines (identical for the same N)."""
+    cfg = model_config(args)
+    B = args.batch * tp
+    lens = context_lengths(B, args.ctx_min, args.ctx_max, 0)
+    kv_gb = cfg.n_layers * decode_attention_bytes([L + 1 for L in lens], cfg.n_heads // tp,
+                                                  cfg.n_kv_heads // tp, cfg.head_dim, 2) / 1e9
+    H, hid, inter, V = cfg.n_heads, cfg.hidden_dim, cfg.intermediate_size, cfg.vocab_size
+    w_gb = 2 * (2 * V * hid + cfg.n_layers * (2 * hid * H * cfg.head_dim // tp
+                + 2 * hid * cfg.n_kv_heads * cfg.head_dim // tp + 3 * hid * inter)) / 1e9
+    return {"workload": workload(args), "global_batch": B * (world // tp),
+            "seq_len": f"{args.ctx_min}-{args.ctx_max} context + decode",
+            "parallelism": (f"KV-head tensor parallel over {world} GPUs, one NCCL all-reduce "
+                            f"per layer after o_proj, MLP replicated" if tp > 1 else
+                            f"{world} request-partitioned replicas, no collective"),
+            "cuda_graph": True, "blocks_per_split": args.blocks_per_split,
+            "l2": (f"inputs larger than L2 every step (~{kv_gb:.1f} GB KV + ~{w_gb:.1f} GB "
+                   f"weights per GPU)"),
+            "kv": "context KV synthesised N(0,1) into the pool"}
 
 
 # ------------------------------------------------------------------ clocks
@@ -139,10 +184,22 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU baseline
+def _cpu_model_name() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return ""
+
+
 def cpu_baseline(args, steps: int, warmup: int, seqs: int):
-    """The oracle port of the reference's forward_decode_paged (llama.py:379-475) on the
-    host cores, fp32, all threads: `seqs` of the workload's sequences, `steps` timed
-    decode steps after `warmup` untimed ones."""
+    """The oracle port of the reference's forward_decode_paged (llama.py:379-475: per
+    layer and sequence gather_kv into zero padding, projections, RoPE, write_kv_decode,
+    GQA expansion, masked SDPA, the same order of torch CPU operations) on the host
+    cores, fp32, all threads: `seqs` of the workload's sequences (the same context
+    lengths as the GPU run), `steps` timed decode steps after `warmup` untimed ones."""
     sys.path.insert(0, str(REPO))
     from oracle.model import OracleLlama
     from oracle.paged import OracleBlockAllocator
@@ -175,20 +232,92 @@ def cpu_baseline(args, steps: int, warmup: int, seqs: int):
         last = lg.float().argmax(-1).tolist()
         cur = [x + 1 for x in cur]
     dt = time.perf_counter() - t0
-    cpu_model = ""
-    try:
-        for line in open("/proc/cpuinfo"):
-            if line.startswith("model name"):
-                cpu_model = line.split(":", 1)[1].strip()
-                break
-    except OSError:
-        pass
     return {"value": len(lens) * steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": (f"oracle port of forward_decode_paged, fp32, {len(lens)} of the "
                        f"{args.batch} sequences (contexts {min(lens)}-{max(lens)}), {steps} timed "
-                       f"steps after {warmup} warm-up, full {cfg.n_layers}-layer geometry, "
-                       f"CPU {cpu_model}"),
+                       f"step(s) after {warmup} warm-up, full {cfg.n_layers}-layer geometry, "
+                       f"CPU {_cpu_model_name()}"),
             "seconds": dt}
+
+
+def config1_inputs(batch: int, seed: int = 0, num_blocks: int = 512):
+    """The single-op decode case: `batch` sequences with cached lengths U{17..1024}
+    (torch.randint(17, 1025), seed 0), 16-token blocks from a random permutation of the
+    pool (512 blocks, or as many as the batch needs), H=32 / Kh=8 / D=64, q and the pool
+    N(0,1) fp32; the new token is already in the pool, so each sequence sees L+1 keys."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(17, 1025, (batch,), generator=g).tolist()
+    need = sum((L + 1 + 15) // 16 for L in lens)
+    num_blocks = max(num_blocks, need)
+    perm = torch.randperm(num_blocks, generator=g)
+    tables, off = [], 0
+    for L in lens:
+        n = (L + 1 + 15) // 16
+        tables.append(perm[off:off + n].tolist())
+        off += n
+    q = torch.randn(batch, 32, 64, generator=g)
+    kp = torch.randn(num_blocks, 16, 8, 64, generator=g)
+    vp = torch.randn(num_blocks, 16, 8, 64, generator=g)
+    return q, kp, vp, tables, [L + 1 for L in lens]
+
+
+def config1_cpu(warmup: int = 3, reps: int = 50):
+    """The attention section of the reference's forward_decode_paged on the CPU
+    (gather_kv -> pad -> GQA expand -> masked SDPA, llama.py:421-469, as the oracle
+    port restates it), fp32, batch 8: ms per op (mean of `reps` after `warmup`) and
+    algorithmic GB/s."""
+    sys.path.insert(0, str(REPO))
+    from oracle import attention as OA
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, kp, vp, tables, lk = config1_inputs(8)
+    for _ in range(warmup):
+        OA.decode_attention_from_pool(q, kp, vp, tables, lk)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        OA.decode_attention_from_pool(q, kp, vp, tables, lk)
+    ms = (time.perf_counter() - t0) / reps * 1e3
+    nbytes = decode_attention_bytes(lk, 32, 8, 64, 4)
+    return {"ms_per_op": ms, "gb_s": nbytes / (ms / 1e3) / 1e9, "algorithmic_bytes": nbytes,
+            "cores": os.cpu_count() or 1, "kind": "port", "reps": reps, "warmup": warmup}
+
+
+def config1_gpu(dev, reps: int = 20):
+    """The same op on the GPU (as_paged_decode_attention): fp32 at batch 8 (the case
+    itself) and bf16 at batch 8 / 64 / 256 with the same length distribution.  Each
+    launch is timed alone with CUDA events after a 256 MB write that evicts L2, so the
+    KV comes from HBM as it would in a step."""
+    from agentserve_b200 import ops
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for dtype, batches in ((torch.float32, (8,)), (torch.bfloat16, (8, 64, 256))):
+        for B in batches:
+            q, kp, vp, tables, lk = config1_inputs(B)
+            q, kp, vp = q.to(dev, dtype), kp.to(dev, dtype), vp.to(dev, dtype)
+            w = max(len(t) for t in tables)
+            bt = torch.zeros(B, w, dtype=torch.int32)
+            for i, t in enumerate(tables):
+                bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+            bt = bt.to(dev)
+            lkt = torch.tensor(lk, dtype=torch.int32, device=dev)
+            ws = ops.new_decode_workspace(B, 32, 8, 64, w, 0, dev)
+            o = torch.empty(B, 32 * 64, dtype=dtype, device=dev)
+            for _ in range(3):
+                ops.paged_decode_attention(q, kp, vp, bt, lkt, 0.125, 0, ws, out=o)
+            tot = 0.0
+            for _ in range(reps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                ops.paged_decode_attention(q, kp, vp, bt, lkt, 0.125, 0, ws, out=o)
+                e1.record()
+                torch.cuda.synchronize()
+                tot += e0.elapsed_time(e1)
+            ms = tot / reps
+            nbytes = decode_attention_bytes(lk, 32, 8, 64, 4 if dtype == torch.float32 else 2)
+            tag = f"{'fp32' if dtype == torch.float32 else 'bf16'}_b{B}"
+            out[tag] = {"us_per_op": ms * 1e3, "gb_s": nbytes / (ms / 1e3) / 1e9,
+                        "algorithmic_bytes": nbytes, "keys": sum(lk)}
+    return out
 
 
 # ------------------------------------------------------------------ helpers
@@ -286,6 +415,410 @@ def measured_bf16_peak():
     return 1590.0, "fallback"
 
 
+# ------------------------------------------------------------------ engine workloads
+class _Classes:
+    """Synthetic request classes for the engine workloads: the prompt text's first word
+    is the class (the engine's difficulty classifier hook), its second the predicted
+    output length (the output-length predictor hook)."""
+    EST = {"easy": (0, 20), "medium": (1, 100), "hard": (2, 256)}
+
+    def classify(self, prompt):
+        from types import SimpleNamespace
+        name = prompt.split()[0]
+        prio, est = self.EST[name]
+        return SimpleNamespace(level=SimpleNamespace(value=name), priority=prio,
+                               estimated_output_tokens=est)
+
+    def predict(self, prompt):
+        return float(prompt.split()[1])
+
+    def update(self, prompt, n):
+        pass
+
+
+def _lognormal_len(rng, median, lo=16, hi=4096, sigma=0.5):
+    import numpy as np
+    return int(np.clip(round(rng.lognormal(math.log(median), sigma)), lo, hi))
+
+
+def _prefill_timer(eng):
+    """Wrap the engine model's batched prefill to time it (host clock around the call,
+    which ends with the first tokens' device-to-host copy) and add up the attention
+    FLOPs of every prefill batch (4*H*D*(T*P + T(T+1)/2) per request)."""
+    st = {"s": 0.0, "attn_flops": 0, "new_tokens": 0, "calls": 0}
+    m = eng.model
+    inner = m.prefill_paged_greedy
+    H, D = m.H, m.D
+
+    def timed(token_ids, num_cached, allocator, request_ids):
+        t0 = time.perf_counter()
+        out = inner(token_ids, num_cached, allocator, request_ids)
+        st["s"] += time.perf_counter() - t0
+        for toks, c in zip(token_ids, num_cached):
+            T = max(1, len(toks) - c)
+            st["attn_flops"] += 4 * H * D * (T * c + T * (T + 1) // 2) * m.config.n_layers
+            st["new_tokens"] += T
+        st["calls"] += 1
+        return out
+
+    m.prefill_paged_greedy = timed
+    return st
+
+
+def _engine_summary(eng, wall, pst, extra):
+    met = eng.metrics
+    lat = {}
+    for cls in ("easy", "medium", "hard"):
+        rs = [r for r in eng.completed_requests if r.difficulty == cls]
+        if rs:
+            lat[cls] = {"n": len(rs), "mean_latency_s": statistics.mean(r.latency for r in rs),
+                        "mean_ttft_s": statistics.mean(r.ttft for r in rs)}
+    out = {"wall_s": wall, "steps": met.steps, "requests": met.completed_requests,
+           "prompt_tokens": met.total_prompt_tokens, "output_tokens": met.total_output_tokens,
+           "output_tok_s": met.total_output_tokens / wall,
+           "engine_throughput_tok_s": (met.total_prompt_tokens + met.total_output_tokens) / wall,
+           "prefill": {"seconds": pst["s"], "calls": pst["calls"], "new_tokens": pst["new_tokens"],
+                       "attention_flops": pst["attn_flops"],
+                       "attention_tflops_over_prefill_time":
+                           pst["attn_flops"] / max(pst["s"], 1e-9) / 1e12},
+           "per_class": lat}
+    out.update(extra)
+    return out
+
+
+def engine_mixed(args, dev, model):
+    """Mixed ragged prefill + decode: 100 agent requests at t=0 (64 easy: prompts
+    lognormal median 300, outputs U[10,30]; 27 medium: 800, U[100,300]; 9 hard: 1500,
+    U[500,1000]; sigma 0.5, clipped to [16, 4096]), batch cap 32, overflow 1.25,
+    priority + relative (combined) batching, EOS off, through B200Engine."""
+    import numpy as np
+    from agentserve_b200 import B200Engine, Request
+    rng = np.random.default_rng(0)
+    spec = [("easy", 64, 300, (10, 30)), ("medium", 27, 800, (100, 300)),
+            ("hard", 9, 1500, (500, 1000))]
+    reqs = []
+    for cls, n, med, (lo, hi) in spec:
+        for _ in range(n):
+            L = _lognormal_len(rng, med)
+            out = int(rng.integers(lo, hi + 1))
+            est = _Classes.EST[cls][1] + int(rng.integers(0, 17))
+            reqs.append(Request(prompt=f"{cls} {est} synthetic agent call",
+                                token_ids=rng.integers(3, 128000, L).tolist(), max_tokens=out,
+                                request_id=f"m{len(reqs)}"))
+    blocks = sum(-(-(len(r.token_ids) + r.max_tokens) // 16) for r in reqs) + 64
+    eng = B200Engine(model.config, model=model, max_batch_size=32, max_prefill_per_step=4,
+                     num_cache_blocks=blocks, eos_token_id=-1, use_combined_batching=True,
+                     classifier=_Classes(), predictor=_Classes(), max_seqs=256)
+    pst = _prefill_timer(eng)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    eng.generate(reqs, max_steps=100_000)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    del model.prefill_paged_greedy
+    res = _engine_summary(eng, wall, pst, {
+        "workload": "100 synthetic agent requests at t=0 (64 easy / 27 medium / 9 hard, "
+                    "prompts lognormal medians 300 / 800 / 1500, outputs U[10,30] / "
+                    "U[100,300] / U[500,1000]), batch cap 32, overflow 1.25, priority + "
+                    "relative batching, greedy, EOS off",
+        "timing": "host wall clock around engine.generate (every step ends with its tokens "
+                  "copied to the host)"})
+    del eng
+    return res
+
+
+def engine_prefix(args, dev, model, sessions: int, turns: int):
+    """Prefix-cache-heavy multi-turn: `sessions` sessions share a 14,336-token random
+    prefix; turn t's prompt is the previous prompt + its output + a new suffix
+    (lognormal median 600, clipped to 4096); outputs U[32,512].  One prefix-only
+    request warms the cache first.  Batch cap 64; prefix hits share the cached
+    blocks in place."""
+    import numpy as np
+    from agentserve_b200 import B200Engine, Request
+    rng = np.random.default_rng(1)
+    prefix = rng.integers(3, 128000, 14336).tolist()
+    suffix = [[rng.integers(3, 128000, _lognormal_len(rng, 600)).tolist() for _ in range(turns)]
+              for _ in range(sessions)]
+    outs = [[int(rng.integers(32, 513)) for _ in range(turns)] for _ in range(sessions)]
+    longest = 14336 + turns * (4096 + 512)
+    per_turn = [sum(len(suffix[s][t]) + outs[s][t] for s in range(sessions)) for t in range(turns)]
+    blocks = 896 + 2 * sum(-(-p // 16) for p in per_turn) + 64 * sessions + 256
+    eng = B200Engine(model.config, model=model, max_batch_size=64, max_prefill_per_step=4,
+                     num_cache_blocks=blocks, eos_token_id=-1,
+                     max_prefix_cache_entries=4 * sessions * turns + 16,
+                     max_seqs=2 * sessions + 8, max_blocks_per_seq=-(-longest // 16))
+    pst = _prefill_timer(eng)
+    prompts = {}
+
+    def req(rid, toks, n):
+        return Request(prompt="medium 100 session turn", token_ids=toks, max_tokens=n,
+                       request_id=rid)
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    eng.generate([req("warm", prefix, 1)])
+    for s in range(sessions):
+        prompts[(s, 0)] = prefix + suffix[s][0]
+        eng.submit(req(f"s{s}t0", prompts[(s, 0)], outs[s][0]))
+    while eng._incoming or not eng.scheduler.is_finished():
+        for r in eng.step():
+            s, t = (int(x) for x in r.request_id[1:].split("t"))
+            if t + 1 < turns:
+                p = prompts[(s, t)] + list(r.output_token_ids) + suffix[s][t + 1]
+                prompts[(s, t + 1)] = p
+                eng.submit(req(f"s{s}t{t + 1}", p, outs[s][t + 1]))
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    del model.prefill_paged_greedy
+    res = _engine_summary(eng, wall, pst, {
+        "workload": (f"{sessions} sessions x {turns} turns sharing a 14,336-token prefix; "
+                     "per-turn suffix lognormal median 600 (clip 4096), outputs U[32,512]; "
+                     "one prefix-only warm-up request; batch cap 64; greedy, EOS off"),
+        "prefix_hit_rate": eng.metrics.prefix_hit_rate,
+        "prefix_tokens_saved": eng.metrics.prefix_tokens_saved,
+        "timing": "host wall clock from the warm-up request to the last turn"})
+    del eng
+    return res
+
+
+# ------------------------------------------------------------------ decode runs
+class Ranks:
+    """Barriers and cross-rank reductions (no-ops on one GPU)."""
+
+    def __init__(self, world: int, dev):
+        self.world, self.dev = world, dev
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj) -> list:
+        if self.world == 1:
+            return [obj]
+        out = [None] * self.world
+        torch.distributed.all_gather_object(out, obj)
+        return out
+
+
+def build_model(cfg, dev, tp: int, rank: int, group=None):
+    """Random-init N(0, 0.02) weights of the architecture, seeded; under KV-head TP the
+    sharded projections get per-rank seeds and everything else the same seed on every
+    rank (as replicated weights must be)."""
+    from agentserve_b200 import B200LlamaModel
+    model = B200LlamaModel(cfg, dtype=torch.bfloat16, device=dev, tp_size=tp,
+                           tp_rank=rank if tp > 1 else 0, tp_group=group)
+    sharded = ("q_proj", "k_proj", "v_proj", "o_proj")
+    with torch.no_grad():
+        for i, (n, p) in enumerate(model.named_parameters()):
+            if p.dim() == 2:
+                own = tp > 1 and any(k in n for k in sharded)
+                g = torch.Generator(device=dev).manual_seed(
+                    1000 + i + (rank if (tp == 1 or own) else 0) * 100003)
+                p.normal_(0.0, 0.02, generator=g)
+    model.eval()
+    model.fuse_projections_()
+    return model
+
+
+class DecodeRun:
+    """One decode batch resident on this GPU: its pool (context KV synthesised
+    N(0,1)), block tables and a self-advancing captured decode step."""
+
+    def __init__(self, model, lens, horizon: int, bps: int, seed: int,
+                 token_seed: int | None = None):
+        from agentserve_b200 import DeviceBlockAllocator
+        cfg = model.config
+        dev = model.device
+        self.model, self.lens, self.bps = model, list(lens), bps
+        self.B = len(lens)
+        nblk = [(L + horizon + 15) // 16 for L in lens]
+        self.alloc = DeviceBlockAllocator(sum(nblk), 16, cfg.n_layers, model.Kh, cfg.head_dim,
+                                          dtype=torch.bfloat16, device=dev, max_seqs=self.B,
+                                          max_blocks_per_seq=max(nblk))
+        gen = torch.Generator(device=dev).manual_seed(77 + seed)
+        self.alloc.kv_pool.normal_(0.0, 1.0, generator=gen)
+        self.rids = [f"s{i}" for i in range(self.B)]
+        for r, n in zip(self.rids, nblk):
+            self.alloc.allocate(r, n)
+        self.rows = self.alloc.rows_for(self.rids)
+        self.max_blocks = max(nblk)
+        # under KV-head TP every rank must feed the same tokens (token_seed shared)
+        ts = seed if token_seed is None else token_seed
+        self.tokens0 = torch.randint(3, cfg.vocab_size, (self.B,),
+                                     generator=torch.Generator().manual_seed(7 + ts)).tolist()
+        self.cur = list(lens)
+        self.last = self.tokens0
+        self.graph = None
+
+    def timed_steps(self, ranks: Ranks, steps: int, warmup: int, clocks=None) -> float:
+        """K replays of the captured step (CUDA events on the launching stream, barrier
+        and synchronize on both sides); returns this rank's milliseconds."""
+        from agentserve_b200 import DecodeGraph
+        self.graph = DecodeGraph(self.model, self.alloc, self.B, self.max_blocks, self.bps,
+                                 advance=True)
+        self.graph.capture(self.last, self.cur, self.rows)
+        for _ in range(warmup):
+            self.graph.replay()
+        torch.cuda.synchronize()
+        if clocks is not None:
+            clocks.start()
+        ranks.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            self.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        ms = e0.elapsed_time(e1)
+        self.cur = [L + warmup + steps for L in self.cur]
+        self.last = self.graph.next_tokens.cpu().tolist()
+        self.graph.release()
+        self.graph = None
+        return ms
+
+    def e2e_steps(self, ranks: Ranks, steps: int) -> float:
+        """`steps` decode steps through forward_decode_paged(host lists) + greedy + a
+        device-to-host read of the tokens, host wall clock; returns seconds."""
+        from agentserve_b200 import greedy
+        m = self.model
+        for _ in range(2):  # captures forward_decode_paged's graph for this batch
+            lg, _ = m.forward_decode_paged(self.last, self.cur, self.cur, self.alloc, self.rids)
+            self.last = greedy(lg).cpu().tolist()
+            self.cur = [x + 1 for x in self.cur]
+        ranks.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            lg, _ = m.forward_decode_paged(self.last, self.cur, self.cur, self.alloc, self.rids)
+            self.last = greedy(lg).cpu().tolist()
+            self.cur = [x + 1 for x in self.cur]
+        torch.cuda.synchronize()
+        return time.perf_counter() - t0
+
+    def attention_alone(self, reps_per_layer: int = 3) -> dict:
+        """The paged decode attention kernel alone: consecutive launches cycle through
+        the layers' planes so none reuses L2; mean launch time and algorithmic bytes."""
+        from agentserve_b200 import ops
+        m, cfg, dev = self.model, self.model.config, self.model.device
+        seq_lens = torch.tensor(self.cur, dtype=torch.int32, device=dev)
+        rows_t = torch.tensor(self.rows, dtype=torch.int32, device=dev)
+        pk = ops.pack_decode(self.alloc.block_tables, seq_lens, rows_t, self.max_blocks)
+        q = torch.randn(self.B, m.H, cfg.head_dim, device=dev, dtype=torch.bfloat16)
+        ws = ops.new_decode_workspace(self.B, m.H, m.Kh, cfg.head_dim, self.max_blocks,
+                                      self.bps, dev)
+        out = torch.empty(self.B, m.H * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+        L = cfg.n_layers
+        for li in range(L):
+            ops.paged_decode_attention(q, self.alloc.k_plane(li), self.alloc.v_plane(li),
+                                       pk.block_tables, pk.seq_lens_k, m.scale, self.bps, ws,
+                                       out=out)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for i in range(reps_per_layer * L):
+            li = i % L
+            ops.paged_decode_attention(q, self.alloc.k_plane(li), self.alloc.v_plane(li),
+                                       pk.block_tables, pk.seq_lens_k, m.scale, self.bps, ws,
+                                       out=out)
+        a1.record()
+        torch.cuda.synchronize()
+        ms = a0.elapsed_time(a1) / (reps_per_layer * L)
+        lk = [x + 1 for x in self.cur]
+        nbytes = decode_attention_bytes(lk, m.H, m.Kh, cfg.head_dim, 2)
+        return {"launch_ms": ms, "algorithmic_bytes_per_launch": nbytes,
+                "achieved_gb_s": nbytes / (ms / 1e3) / 1e9}
+
+    def free(self):
+        if self.graph is not None:
+            self.graph.release()
+        self.graph = None
+        self.alloc = None
+
+
+def affinity() -> dict:
+    try:
+        cores = sorted(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return {}
+    return {"cores": len(cores), "first": cores[0], "last": cores[-1]}
+
+
+def allreduce_ms(ranks: Ranks, B: int, hidden: int, dev, reps: int = 50) -> float:
+    """One NCCL all-reduce of the [B, hidden] bf16 o_proj output, timed alone."""
+    t = torch.randn(B, hidden, device=dev, dtype=torch.bfloat16)
+    for _ in range(5):
+        torch.distributed.all_reduce(t)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        torch.distributed.all_reduce(t)
+    e1.record()
+    torch.cuda.synchronize()
+    return ranks.max(e0.elapsed_time(e1) / reps)
+
+
+def config5(args, dev, ranks: Ranks, rank: int, world: int) -> dict:
+    """The 8B geometry (32 layers, hidden 4096, 32/8 heads, head_dim 128, FFN 14336),
+    contexts U{1024..32768}: (a) request-partitioned replicas, 32 sequences per GPU
+    (8 GPUs x 32 = the 256-sequence configuration); (b) for N > 1, KV-head tensor
+    parallelism over the N GPUs with one NCCL all-reduce of the [B, 4096] o_proj output
+    per layer, on min(256, 32 N) sequences (each GPU holds Kh/N KV heads of every
+    sequence: the same per-GPU KV as a replica)."""
+    cfg = config_8b()
+    steps, warm = args.config5_steps, 3
+    res = {"workload": ("8B geometry, bf16, random-init N(0,0.02), contexts U{1024..32768}, "
+                        "16-token blocks, greedy, CUDA-graph steps")}
+    model = build_model(cfg, dev, 1, rank)
+    run = DecodeRun(model, context_lengths(32, 1024, 32768, seed=500 + rank), warm + steps + 4,
+                    0, seed=500 + rank)
+    ms = ranks.max(run.timed_steps(ranks, steps, warm))
+    att = run.attention_alone(reps_per_layer=1)
+    res["replicas"] = {"sequences_per_gpu": 32, "n_gpus": world,
+                       "value": world * 32 * steps / (ms / 1e3), "unit": "tok/s",
+                       "ms_per_step": ms / steps,
+                       "attention_gb_s": att["achieved_gb_s"],
+                       "attention_frac": att["achieved_gb_s"] / measured_peaks()[0]}
+    run.free()
+    del run, model
+    gc.collect()
+    torch.cuda.empty_cache()
+    if world > 1:
+        B = min(256, 32 * world)
+        model = build_model(cfg, dev, world, rank, group=torch.distributed.group.WORLD)
+        run = DecodeRun(model, context_lengths(B, 1024, 32768, seed=600), warm + steps + 4, 0,
+                        seed=600 + rank, token_seed=600)
+        ms = ranks.max(run.timed_steps(ranks, steps, warm))
+        att = run.attention_alone(reps_per_layer=1)
+        ar = allreduce_ms(ranks, B, cfg.hidden_dim, dev)
+        step_ms = ms / steps
+        res["tensor_parallel"] = {
+            "sequences": B, "n_gpus": world, "kv_heads_per_gpu": cfg.n_kv_heads // world,
+            "value": B * steps / (ms / 1e3), "unit": "tok/s", "ms_per_step": step_ms,
+            "attention_gb_s_per_gpu": att["achieved_gb_s"],
+            "attention_frac": att["achieved_gb_s"] / measured_peaks()[0],
+            "allreduce_ms_alone": ar,
+            "allreduce_share_of_step": cfg.n_layers * ar / step_ms,
+            "collective": f"NCCL all-reduce (sum, bf16) of [{B}, {cfg.hidden_dim}] after "
+                          f"o_proj, {cfg.n_layers} per step, captured in the step's graph"}
+        model.release_decode_graphs()
+        run.free()
+        del run, model
+        gc.collect()
+        torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------ main arms
 def run_reference(args):
     rank, _, world = dist_env()
@@ -293,11 +826,11 @@ def run_reference(args):
         return
     cb = cpu_baseline(args, steps=max(1, min(args.steps, args.cpu_sample_steps)),
                       warmup=min(args.warmup, 1), seqs=args.cpu_sample_seqs)
+    tp = world if args.tp else 1
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": workload(args),
-                                            "sample": cb["sample"]},
+            "data": "synthetic", "config": line_config(args, world, tp),
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -310,184 +843,135 @@ def run_b200(args):
     dev = torch.device("cuda", local_rank)
     if world > 1:
         import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
-    from agentserve_b200 import B200LlamaModel, DecodeGraph, DeviceBlockAllocator, greedy, ops
-
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    from agentserve_b200 import ops
+    ranks = Ranks(world, dev)
     cfg = model_config(args)
     tp = world if args.tp else 1
     # replicas: every rank decodes its own `batch` sequences; KV-head TP: all ranks
     # decode the same batch * world sequences, each holding 1/world of the KV heads
     B = args.batch * tp
-    model = B200LlamaModel(cfg, dtype=torch.bfloat16, device=dev, tp_size=tp,
-                           tp_rank=rank if tp > 1 else 0)
-    sharded = ("q_proj", "k_proj", "v_proj", "o_proj")
-    with torch.no_grad():
-        for i, (n, p) in enumerate(model.named_parameters()):
-            if p.dim() == 2:
-                own = tp > 1 and any(k in n for k in sharded)
-                g = torch.Generator(device=dev).manual_seed(
-                    1000 + i + (rank if (tp == 1 or own) else 0) * 100003)
-                p.normal_(0.0, 0.02, generator=g)
-    gen = torch.Generator(device=dev).manual_seed(77 + (rank if tp == 1 else 0))
-    model.eval()
-    model.fuse_projections_()
-
+    group = torch.distributed.group.WORLD if tp > 1 else None
+    model = build_model(cfg, dev, tp, rank, group)
     lens = context_lengths(B, args.ctx_min, args.ctx_max, seed=rank if tp == 1 else 0)
     horizon = args.warmup + args.steps + args.e2e_steps + 4
-    nblk = [(L + horizon + 15) // 16 for L in lens]
-    alloc = DeviceBlockAllocator(sum(nblk), 16, cfg.n_layers, model.Kh, cfg.head_dim,
-                                 dtype=torch.bfloat16, device=dev, max_seqs=B,
-                                 max_blocks_per_seq=max(nblk))
-    alloc.kv_pool.normal_(0.0, 1.0, generator=gen)  # synthesised context KV
-    rids = [f"s{i}" for i in range(B)]
-    for r, n in zip(rids, nblk):
-        alloc.allocate(r, n)
-    rows = alloc.rows_for(rids)
-    max_blocks = max(nblk)
-    bps = args.blocks_per_split  # 0: balanced persistent partition
-    model.decode_blocks_per_split = bps
-    tokens0 = torch.randint(3, cfg.vocab_size, (B,),
-                            generator=torch.Generator().manual_seed(7 + (rank if tp == 1 else 0)))
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
+    run = DecodeRun(model, lens, horizon, args.blocks_per_split, seed=rank if tp == 1 else 0)
 
     # ---------------- device-resident decode steps (CUDA graph, self-advancing)
-    graph = DecodeGraph(model, alloc, B, max_blocks, bps, advance=True)
-    graph.capture(tokens0.tolist(), lens, rows)
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
     clocks = ClockSampler(local_rank)
-    clocks.start()
-    barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
-        graph.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    barrier()
+    my_ms = run.timed_steps(ranks, args.steps, args.warmup, clocks=clocks)
     clk = clocks.stop()
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms = ranks.max(my_ms)
     value = (world // tp) * B * args.steps / (ms / 1e3)
+    per_rank = ranks.gather({"rank": rank, "ms_per_step": my_ms / args.steps,
+                             "affinity": affinity()})
 
     # ---------------- end to end through forward_decode_paged with host lists
-    cur = [L + args.warmup + args.steps for L in lens]
-    last = graph.next_tokens.cpu().tolist()
-    graph.release()
-    del graph
-    torch.cuda.synchronize()
-    e2e_steps = max(3, args.e2e_steps)
-    for _ in range(2):  # capture forward_decode_paged's graph for this batch
-        lg, _ = model.forward_decode_paged(last, cur, cur, alloc, rids)
-        last = greedy(lg).cpu().tolist()
-        cur = [x + 1 for x in cur]
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps - 2):
-        lg, _ = model.forward_decode_paged(last, cur, cur, alloc, rids)
-        last = greedy(lg).cpu().tolist()
-        cur = [x + 1 for x in cur]
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e_value = (world // tp) * B * (e2e_steps - 2) / e2e_s
+    e2e_n = max(1, args.e2e_steps - 2)
+    e2e_s = ranks.max(run.e2e_steps(ranks, e2e_n))
+    e2e_value = (world // tp) * B * e2e_n / e2e_s
 
     # ---------------- paged decode attention kernel alone (roofline)
-    seq_lens = torch.tensor(cur, dtype=torch.int32, device=dev)
-    rows_t = torch.tensor(rows, dtype=torch.int32, device=dev)
-    pk = ops.pack_decode(alloc.block_tables, seq_lens, rows_t, max_blocks)
-    q = torch.randn(B, model.H, cfg.head_dim, device=dev, dtype=torch.bfloat16)
-    ws = ops.new_decode_workspace(B, model.H, model.Kh, cfg.head_dim, max_blocks, bps, dev)
-    out = torch.empty(B, model.H * cfg.head_dim, device=dev, dtype=torch.bfloat16)
-    reps = 3 * cfg.n_layers
-    for li in range(cfg.n_layers):  # warm
-        ops.paged_decode_attention(q, alloc.k_plane(li), alloc.v_plane(li), pk.block_tables,
-                                   pk.seq_lens_k, model.scale, bps, ws, out=out)
-    torch.cuda.synchronize()
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record()
-    for i in range(reps):  # consecutive launches read different layers' planes (> L2)
-        li = i % cfg.n_layers
-        ops.paged_decode_attention(q, alloc.k_plane(li), alloc.v_plane(li), pk.block_tables,
-                                   pk.seq_lens_k, model.scale, bps, ws, out=out)
-    a1.record()
-    torch.cuda.synchronize()
-    attn_ms = a0.elapsed_time(a1) / reps
-    lk = [x + 1 for x in cur]
-    abytes = decode_attention_bytes(lk, model.H, model.Kh, cfg.head_dim, 2)
-    achieved = abytes / (attn_ms / 1e3) / 1e9
+    att = run.attention_alone()
     peak, peak_kind = measured_peaks()
-    pf = measure_prefill(dev) if not args.no_prefill and tp == 1 else None
-    pf128 = measure_prefill(dev, D=128) if not args.no_prefill and tp == 1 else None
     bits = ops.device_status(clear=True)
+    model.release_decode_graphs()
+    run.free()
+    del run
+    gc.collect()
+    torch.cuda.empty_cache()
 
-    if world > 1:
-        torch.distributed.barrier()
+    # ---------------- the same 64 sequences split over the N GPUs (strong scaling)
+    strong = None
+    if world > 1 and tp == 1 and not args.no_strong:
+        all_lens = context_lengths(args.batch, args.ctx_min, args.ctx_max, seed=0)
+        mine = all_lens[rank::world]
+        srun = DecodeRun(model, mine, args.warmup + args.steps + 4, args.blocks_per_split,
+                         seed=900 + rank)
+        s_ms = srun.timed_steps(ranks, args.steps, args.warmup)
+        s_max = ranks.max(s_ms)
+        strong = {"sequences_total": args.batch, "sequences_per_gpu": len(mine),
+                  "value": args.batch * args.steps / (s_max / 1e3), "unit": "tok/s",
+                  "ms_per_step": s_max / args.steps,
+                  "per_rank_ms_per_step": [x / args.steps for x in ranks.gather(s_ms)],
+                  "note": "strong scaling: total work fixed at the 64 sequences of one GPU's "
+                          "workload, split round-robin over the N GPUs"}
+        srun.free()
+        del srun
+        model.release_decode_graphs()
+        gc.collect()
+        torch.cuda.empty_cache()
+
+    # ---------------- 8B geometry: replicas, and KV-head TP over the N GPUs
+    c5 = None
+    if args.model == "1b" and tp == 1 and not args.no_config5:
+        c5 = config5(args, dev, ranks, rank, world)
+        bits |= ops.device_status(clear=True)
+
+    pf = pf128 = c1 = engines = None
+    if rank == 0 and world == 1 and tp == 1:
+        if not args.no_prefill:
+            pf = measure_prefill(dev)
+            pf128 = measure_prefill(dev, D=128)
+        if not args.no_config1:
+            c1 = {"cpu": config1_cpu(), "gpu": config1_gpu(dev),
+                  "case": "one paged decode-attention op: 8 sequences, cached lengths "
+                          "U{17..1024} (seed 0), 512-block pool, 32/8 heads, head_dim 64, "
+                          "fp32; the GPU also at batch 64 / 256 and in bf16"}
+        if not args.no_engine and args.model == "1b":
+            engines = {"mixed_requests": engine_mixed(args, dev, model),
+                       "prefix_cache_sessions": engine_prefix(args, dev, model,
+                                                              args.engine_sessions,
+                                                              args.engine_turns)}
+        bits |= ops.device_status(clear=True)
+
+    ranks.barrier()
     if rank == 0:
-        kv_gb = cfg.n_layers * decode_attention_bytes(lk, model.H, model.Kh,
-                                                      cfg.head_dim, 2) / 1e9
-        w_gb = sum(p.numel() for p in model.parameters()) * 2 / 1e9
         traffic = load_traffic() if args.model == "1b" else None
         traffic_launch = None
         if traffic:
-            traffic_launch = (traffic["dram_bytes_per_launch"] * abytes
+            traffic_launch = (traffic["dram_bytes_per_launch"] * att["algorithmic_bytes_per_launch"]
                               / traffic["algorithmic_bytes_captured"])
+        bf16_peak, bf16_kind = measured_bf16_peak()
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": workload(args), "global_batch": B * (world // tp),
-                       "seq_len": f"{args.ctx_min}-{args.ctx_max} context + decode",
-                       "parallelism": (f"KV-head tensor parallel over {world} GPUs, one NCCL "
-                                       f"all-reduce per layer after o_proj, MLP replicated"
-                                       if tp > 1 else
-                                       f"{world} request-partitioned replicas, no collective"),
-                       "cuda_graph": True, "blocks_per_split": bps,
-                       "l2": (f"inputs larger than L2 every step (~{kv_gb:.1f} GB KV + "
-                              f"~{w_gb:.1f} GB weights)"),
-                       "kv": "context KV synthesised N(0,1) into the pool"},
+            "data": "synthetic", "config": line_config(args, world, tp),
             "roofline": {"kernel": f"paged_decode_attention (bf16, D={cfg.head_dim}, GQA "
                                    f"{model.H // model.Kh}, {model.Kh} KV heads per GPU)",
-                         "bound": "hbm",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                         "algorithmic_bytes_per_launch": abytes, "launch_ms": attn_ms,
-                         "traffic": traffic_launch,
+                         "bound": "hbm", "achieved": att["achieved_gb_s"], "peak": peak,
+                         "unit": "GB/s", "frac": att["achieved_gb_s"] / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_launch": att["algorithmic_bytes_per_launch"],
+                         "launch_ms": att["launch_ms"], "traffic": traffic_launch,
                          "traffic_source": (traffic or {}).get("source")},
-            "e2e": {"value": e2e_value, "unit": "tok/s", "api": "B200LlamaModel.forward_decode_paged"
-                    "(host lists) + greedy + .cpu()",
+            "e2e": {"value": e2e_value, "unit": "tok/s",
+                    "api": "B200LlamaModel.forward_decode_paged(host lists) + greedy + .cpu()",
                     # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
                     # the greedy int64 tokens out
                     "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8},
             # per step: pack + first RMSNorm + greedy argmax + per layer (RoPE/cache,
             # attention, 2 x add+RMSNorm, SwiGLU); the projections and lm_head are cuBLAS
             "gpu_launches": args.steps * (3 + 5 * cfg.n_layers),
+            "per_rank": per_rank,
+            "strong": strong,
+            "config5": c5,
             "prefill": None if pf is None else {
                 "kernel": "varlen prefill attention, tcgen05 + TMEM (bf16, D=64, GQA 4)",
                 "shape": "prefix 14336 + 600 new tokens per request (prefix-cache workload)",
                 "roofline": {"bound": "tensor", "achieved": pf["8x"]["tflops"],
-                             "peak": measured_bf16_peak()[0], "unit": "TFLOP/s",
-                             "frac": pf["8x"]["tflops"] / measured_bf16_peak()[0],
-                             "peak_source": measured_bf16_peak()[1] + " bf16_tflops (burst)"},
+                             "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": pf["8x"]["tflops"] / bf16_peak,
+                             "peak_source": bf16_kind + " bf16_tflops (burst)"},
                 "one_request": pf["1x"], "eight_requests": pf["8x"],
                 "head_dim_128": {"note": "same shape with the 8B geometry's head_dim 128 "
                                          "(32/8 heads)", "one_request": pf128["1x"],
                                  "eight_requests": pf128["8x"],
-                                 "frac": pf128["8x"]["tflops"] / measured_bf16_peak()[0]}},
+                                 "frac": pf128["8x"]["tflops"] / bf16_peak}},
+            "config1": c1,
+            "engine": engines,
             "clocks": clk, "device_status": bits,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -495,7 +979,7 @@ def run_b200(args):
                               seqs=args.cpu_sample_seqs)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
-    model.release_decode_graphs()  # they captured this group's all-reduce
+    model.release_decode_graphs()  # they may hold this group's all-reduce
     gc.collect()
     torch.cuda.synchronize()
     if world > 1:

@@ -40,6 +40,18 @@ def decode_attention_padded(q: torch.Tensor, k_hist: List[torch.Tensor],
     for b in range(B):
         kp[b, :lens[b]] = k_hist[b].to(q.dtype)
         vp[b, :lens[b]] = v_hist[b].to(q.dtype)
+    return decode_attention_prepadded(q, kp, vp, k_new, v_new, lens)
+
+
+def decode_attention_prepadded(q: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor,
+                               k_new: torch.Tensor, v_new: torch.Tensor,
+                               lens: Sequence[int]) -> torch.Tensor:
+    """The rest of one decode step once the history is padded into kp/vp
+    [B, max_len, Kh, D] (llama.py:441-469): append the new token, expand the KV heads,
+    mask the padding columns, SDPA.  Returns [B, H, D]."""
+    B, H, D = q.shape
+    lens = [int(L) for L in lens]
+    max_len = kp.shape[1]
     k_full = torch.cat([kp, k_new.unsqueeze(1)], dim=1)
     v_full = torch.cat([vp, v_new.unsqueeze(1)], dim=1)
     total = max_len + 1

@@ -19,7 +19,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .attention import decode_attention_padded, flatten_decode_output, prefill_attention
+from .attention import (decode_attention_padded, decode_attention_prepadded, flatten_decode_output,
+                        prefill_attention)
 from .rope import apply_rope, precompute_rope_freqs
 
 
@@ -156,15 +157,24 @@ class OracleLlama(nn.Module):
         dev = self.rope_table.device
         x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
         cs = self.rope_table[torch.tensor(position_offsets, dtype=torch.long, device=dev)]
+        Kh, D = c.n_kv_heads, c.head_dim
+        max_len = max(seq_lens)
         for li, layer in enumerate(self.layers):
-            hist = [allocator.gather_kv(rid, L, li) for rid, L in zip(request_ids, seq_lens)]
+            # llama.py:421-426: the history of every sequence gathered into zero padding,
+            # one sequence at a time, before the projections
+            kp = x.new_zeros(B, max_len, Kh, D)
+            vp = x.new_zeros(B, max_len, Kh, D)
+            for b, (rid, L) in enumerate(zip(request_ids, seq_lens)):
+                k_b, v_b = allocator.gather_kv(rid, L, li)
+                kp[b, :L] = k_b.to(dtype=x.dtype, device=dev)
+                vp[b, :L] = v_b.to(dtype=x.dtype, device=dev)
             h = layer.attn_norm(x)
             q, kn, vn = self._qkv(layer, h, B)
             q = apply_rope(q, cs)
             kn = apply_rope(kn, cs)
             for b, (rid, L) in enumerate(zip(request_ids, seq_lens)):
                 allocator.write_kv_decode(rid, L, li, kn[b], vn[b])
-            attn = decode_attention_padded(q, [k for k, _ in hist], [v for _, v in hist], kn, vn)
+            attn = decode_attention_prepadded(q, kp, vp, kn, vn, seq_lens)
             x = x + layer.attn.o_proj(flatten_decode_output(attn))
             x = x + layer.ffn(layer.ffn_norm(x))
         return self.lm_head(self.norm(x)), None

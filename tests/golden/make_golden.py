@@ -4,7 +4,7 @@ Run in a container where the reference (krishs0404/agentserve) is checked out:
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--reference PATH]
 
-The default PATH is $AGENTSERVE_REFERENCE or /root/reference.  Every array
+PATH (or $AGENTSERVE_REFERENCE) is a checkout of the reference.  Every array
 written here comes from the reference's own code (BlockAllocator, apply_rope,
 precompute_rope_freqs, LlamaModel.forward / forward_decode_batch /
 forward_decode_paged, sample at temperature 0), on seeded inputs that the tests regenerate.  Large inputs
@@ -194,8 +194,11 @@ def gen_models(config_mod, llama, cache, out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("AGENTSERVE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("AGENTSERVE_REFERENCE"),
+                    help="checkout of krishs0404/agentserve (or $AGENTSERVE_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set AGENTSERVE_REFERENCE")
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     cache, config_mod, llama = import_reference(args.reference)
     out: dict = {}
