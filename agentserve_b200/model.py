@@ -61,13 +61,18 @@ class RMSNorm(nn.Module):
 
 
 class _Attn(nn.Module):
-    def __init__(self, c, tp_size: int = 1):
+    def __init__(self, c, tp_size: int = 1, split_o: bool = False):
         super().__init__()
         H, Kh, D = c.n_heads // tp_size, c.n_kv_heads // tp_size, c.head_dim
         self.q_proj = nn.Linear(c.hidden_dim, H * D, bias=False)
         self.k_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
         self.v_proj = nn.Linear(c.hidden_dim, Kh * D, bias=False)
         self.o_proj = nn.Linear(H * D, c.hidden_dim, bias=False)
+        # KV-head TP with the reference's two flattens: prefill feeds o_proj head-major
+        # (llama.py:184), decode dim-major (llama.py:362, 470), so a rank's heads meet
+        # two different column sets of the full o_proj; o_proj holds the decode set and
+        # o_proj_prefill the prefill one
+        self.o_proj_prefill = nn.Linear(H * D, c.hidden_dim, bias=False) if split_o else None
 
 
 class _MLP(nn.Module):
@@ -79,10 +84,10 @@ class _MLP(nn.Module):
 
 
 class _Layer(nn.Module):
-    def __init__(self, c, tp_size: int = 1):
+    def __init__(self, c, tp_size: int = 1, split_o: bool = False):
         super().__init__()
         self.attn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
-        self.attn = _Attn(c, tp_size)
+        self.attn = _Attn(c, tp_size, split_o)
         self.ffn_norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
         self.ffn = _MLP(c)
 
@@ -96,7 +101,9 @@ def shard_state_dict(full: dict, config, tp_size: int, tp_rank: int,
     columns its heads feed.  Those columns are contiguous for the head-major flatten
     (h*D + d), and strided for the reference decode's dim-major flatten (d*H + h):
     the rank's local attention output is d*H_l + h_l, so its o_proj shard is
-    W[:, d*H + r*H_l + h_l] in that order.  Everything else is replicated."""
+    W[:, d*H + r*H_l + h_l] in that order.  With reference_compat the prefill still
+    flattens head-major, so the rank also gets the contiguous shard as
+    attn.o_proj_prefill.weight.  Everything else is replicated."""
     H, Kh, D = config.n_heads, config.n_kv_heads, config.head_dim
     if H % tp_size or Kh % tp_size:
         raise ValueError(f"{tp_size} ranks cannot split {H} query / {Kh} KV heads")
@@ -115,6 +122,11 @@ def shard_state_dict(full: dict, config, tp_size: int, tp_rank: int,
             out[name] = w[tp_rank * Khl * D:(tp_rank + 1) * Khl * D]
         elif name.endswith("attn.o_proj.weight"):
             out[name] = w[:, ocols.to(w.device)]
+            if reference_compat:
+                out[name.replace("o_proj.weight", "o_proj_prefill.weight")] = \
+                    w[:, tp_rank * Hl * D:(tp_rank + 1) * Hl * D]
+        elif name.endswith("attn.o_proj_prefill.weight"):
+            continue
         else:
             out[name] = w
     return {k: v.contiguous() for k, v in out.items()}
@@ -138,7 +150,8 @@ class B200LlamaModel(nn.Module):
         self.tp_size, self.tp_rank, self.tp_group = tp_size, tp_rank, tp_group
         self.H, self.Kh, self.D = c.n_heads // tp_size, c.n_kv_heads // tp_size, c.head_dim
         self.embed = nn.Embedding(c.vocab_size, c.hidden_dim)
-        self.layers = nn.ModuleList([_Layer(c, tp_size) for _ in range(c.n_layers)])
+        split_o = tp_size > 1 and reference_compat
+        self.layers = nn.ModuleList([_Layer(c, tp_size, split_o) for _ in range(c.n_layers)])
         self.norm = RMSNorm(c.hidden_dim, c.rms_norm_eps)
         self.lm_head = nn.Linear(c.hidden_dim, c.vocab_size, bias=False)
         self.to(device=device, dtype=dtype)
@@ -220,15 +233,18 @@ class B200LlamaModel(nn.Module):
             return self._linear(ops.silu_mul(self._linear(h, f._gu_w)), f.down_proj.weight)
         return f.down_proj(F.silu(f.gate_proj(h)) * f.up_proj(h))
 
-    def _run_layers(self, x: torch.Tensor, attention) -> torch.Tensor:
+    def _run_layers(self, x: torch.Tensor, attention, prefill: bool = False) -> torch.Tensor:
         """The decoder stack (llama.py:218-238) with the residual adds fused into the
         next pre-norm: x is the embedding output (updated in place as the residual
-        stream); attention(li, layer, h) returns the attention output fed to o_proj.
-        Returns the final-norm output."""
+        stream); attention(li, layer, h) returns the attention output fed to o_proj
+        (head-major for prefill=True).  Returns the final-norm output."""
         L = len(self.layers)
         h = ops.rmsnorm(x, self.layers[0].attn_norm.weight, self.layers[0].attn_norm.eps)
         for li, layer in enumerate(self.layers):
-            a = self._linear(attention(li, layer, h), layer.attn.o_proj.weight)
+            wo = layer.attn.o_proj.weight
+            if prefill and layer.attn.o_proj_prefill is not None:
+                wo = layer.attn.o_proj_prefill.weight
+            a = self._linear(attention(li, layer, h), wo)
             if self.tp_size > 1:  # row-parallel o_proj: sum the ranks' partial outputs
                 torch.distributed.all_reduce(a, group=self.tp_group)
             h = ops.add_rmsnorm(x, a, layer.ffn_norm.weight, layer.ffn_norm.eps)
@@ -287,7 +303,7 @@ class B200LlamaModel(nn.Module):
             new_cache.append((kf[:total], vf[:total]))
             return ops.varlen_prefill_attention(q, kbuf, vbuf, bt, cu, lk, T, self.scale)
 
-        h = self._run_layers(x, attention)
+        h = self._run_layers(x, attention, prefill=True)
         return self._logits(h), new_cache
 
     # ------------------------------------------------------------------ prefill (paged)
@@ -334,7 +350,7 @@ class B200LlamaModel(nn.Module):
             return ops.varlen_prefill_attention(q, kp, vp, pk.block_tables, pk.cu_seqlens_q,
                                                 pk.seq_lens_k, max_new, self.scale)
 
-        h = self._run_layers(self.embed(tokens), attention)
+        h = self._run_layers(self.embed(tokens), attention, prefill=True)
         last = pk.cu_seqlens_q[1:].long() - 1
         return self._logits(h.index_select(0, last))
 

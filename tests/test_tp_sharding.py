@@ -102,3 +102,29 @@ def test_shard_shapes_and_replication():
     assert torch.equal(sd["layers.0.ffn_norm.weight"], full_weights()["layers.0.ffn_norm.weight"])
     with pytest.raises(ValueError):
         shard_state_dict(full_weights(), CFG, 3, 0)
+
+
+@pytest.mark.parametrize("compat", [True, False])
+def test_o_proj_shards_cover_both_flattens(compat):
+    """With the reference's flattens, prefill feeds o_proj head-major (llama.py:184) and
+    decode dim-major (llama.py:362, 470): the ranks' o_proj (decode) and o_proj_prefill
+    shards must each sum back to the unsharded product."""
+    H, D, hid = CFG.n_heads, CFG.head_dim, CFG.hidden_dim
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(hid, H * D, generator=g)
+    o = torch.randn(5, H, D, generator=g)
+    full = {"layers.0.attn.o_proj.weight": w}
+    want_pre = o.reshape(5, H * D) @ w.T
+    want_dec = (o.transpose(1, 2).reshape(5, H * D) if compat else o.reshape(5, H * D)) @ w.T
+    got_pre = got_dec = 0
+    for r in range(2):
+        s = shard_state_dict(full, CFG, 2, r, compat)
+        ol = o[:, r * H // 2:(r + 1) * H // 2]
+        dec_in = ol.transpose(1, 2).reshape(5, -1) if compat else ol.reshape(5, -1)
+        got_dec = got_dec + dec_in @ s["layers.0.attn.o_proj.weight"].T
+        wp = s.get("layers.0.attn.o_proj_prefill.weight", s["layers.0.attn.o_proj.weight"])
+        got_pre = got_pre + ol.reshape(5, -1) @ wp.T
+    torch.testing.assert_close(got_pre, want_pre, rtol=0, atol=1e-4)
+    torch.testing.assert_close(got_dec, want_dec, rtol=0, atol=1e-4)
+    assert ("layers.0.attn.o_proj_prefill.weight" in shard_state_dict(full, CFG, 2, 0, compat)) \
+        == compat
