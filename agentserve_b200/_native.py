@@ -70,6 +70,10 @@ SIGNATURES = {
     "as_silu_mul": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P]),
     "as_block_copy": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _I64, _I32, _I32,
                                      _P]),
+    "as_rope_paged_decode_attention": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _I64, _P, _P,
+                                                      _P, _I32, _P, _P, _P, _I64, _P, _I32, _I32,
+                                                      _I32, _I32, _I32, _I32, _I32, _F32, _I32,
+                                                      _P, _SZ, _I32, _I32, _P]),
     "as_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "as_debug_starve_next_launch": (ctypes.c_int, [ctypes.c_int]),
 }

@@ -229,6 +229,96 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qb)[D / 16][2], const T*
   }
 }
 
+// The decode step's new token, for the variant that also does the RoPE + cache write
+// of that token (as_rope_paged_decode_attention): unrotated q / k / v rows, their
+// position and pool slot, the fp32 cos||sin table and the pool planes.
+template <typename T>
+struct NewToken {
+  const T* q;
+  int64_t q_stride;
+  const T* k;
+  int64_t k_stride;
+  const T* v;
+  int64_t v_stride;
+  const int64_t* positions;
+  const int64_t* slot_mapping;
+  const float* cos_sin;
+  int table_len;
+  T* k_cache;
+  T* v_cache;
+  int64_t num_slots;
+};
+
+// Rotate-half RoPE of element d of one head row x (llama.py:80-99), each product and
+// the sum / difference rounded on its own in fp32 as torch evaluates it, so the
+// result has the bits of the separate RoPE kernel's.
+template <typename T, int D>
+__device__ __forceinline__ float rope_elem(const T* __restrict__ x, const float* __restrict__ cs,
+                                           int d) {
+  constexpr int half = D / 2;
+  const int j = d < half ? d : d - half;
+  const float a = Elem<T>::to_f32(x[j]);
+  const float b = Elem<T>::to_f32(x[j + half]);
+  const float c = __ldg(cs + j), sn = __ldg(cs + half + j);
+  return d < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn))
+                  : __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
+}
+
+// load_q_frags for an unrotated q: each element is rotated for the token's position on
+// the way in (a position outside the table leaves q as it is, as the RoPE kernel does).
+template <typename T, int D>
+__device__ __forceinline__ void load_q_frags_rope(uint32_t (&qb)[D / 16][2], const NewToken<T>& nt,
+                                                  int b, int g, int group, int lane) {
+  const int gq = lane >> 2, tq = lane & 3;
+  const bool has_head = gq < group;
+  const T* qrow = nt.q + int64_t(b) * nt.q_stride + int64_t(g * group + (has_head ? gq : 0)) * D;
+  const int64_t pos = nt.positions[b];
+  const bool rot = pos >= 0 && pos < nt.table_len;
+  const float* cs = nt.cos_sin + (rot ? pos : 0) * int64_t(D);
+  auto val = [&](int d) -> float {
+    return rot ? rope_elem<T, D>(qrow, cs, d) : Elem<T>::to_f32(qrow[d]);
+  };
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int e = 16 * kk + 2 * tq;
+    qb[kk][0] = has_head ? pack2<T>(val(e), val(e + 1)) : 0u;
+    qb[kk][1] = has_head ? pack2<T>(val(e + 8), val(e + 9)) : 0u;
+  }
+}
+
+// The new token's rotated k and its v into pool slot slot_mapping[b] for KV head g, by
+// one warp; the async-proxy fence makes the stores visible to the TMA loads that
+// follow.  A bad position skips the token (flagged), a slot past the pool is flagged
+// and skipped, a negative slot skipped silently: as the RoPE kernel does.
+template <typename T, int D>
+__device__ __forceinline__ void write_new_token(const NewToken<T>& nt, int b, int g, int Kh,
+                                                int lane, int* status) {
+  constexpr int half = D / 2;
+  const int64_t pos = nt.positions[b];
+  if (pos < 0 || pos >= nt.table_len) {
+    if (lane == 0 && g == 0) flag_status(status, kStatusBadPosition);
+    return;
+  }
+  const int64_t slot = nt.slot_mapping[b];
+  if (slot < 0 || slot >= nt.num_slots) {
+    if (slot >= nt.num_slots && lane == 0 && g == 0) flag_status(status, kStatusBadSlot);
+    return;
+  }
+  const T* kr = nt.k + int64_t(b) * nt.k_stride + int64_t(g) * D;
+  const T* vr = nt.v + int64_t(b) * nt.v_stride + int64_t(g) * D;
+  T* kd = nt.k_cache + (slot * Kh + g) * int64_t(D);
+  T* vd = nt.v_cache + (slot * Kh + g) * int64_t(D);
+  const float* cs = nt.cos_sin + pos * int64_t(D);
+#pragma unroll
+  for (int j = lane; j < half; j += 32) {
+    kd[j] = Elem<T>::from_f32(rope_elem<T, D>(kr, cs, j));
+    kd[j + half] = Elem<T>::from_f32(rope_elem<T, D>(kr, cs, j + half));
+    vd[j] = vr[j];
+    vd[j + half] = vr[j + half];
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ===========================================================================
 // Fast path: TMA + mma.sync, bf16/fp16, D in {64, 128}
 // ===========================================================================
@@ -262,7 +352,9 @@ struct FastCfg {
       kMaxBlocksPerSplit * 4;
 };
 
-template <typename T, int D>
+// kNewToken: q arrives unrotated and this kernel also does the new token's RoPE and
+// cache write (nt); otherwise q is already rotated and the token already in the pool.
+template <typename T, int D, bool kNewToken>
 __global__ void __launch_bounds__(FastCfg<D>::kThreads)
 decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, T* __restrict__ out,
@@ -270,7 +362,7 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    int64_t bt_stride, const int32_t* __restrict__ seq_lens_k, int H, int Kh,
                    int group, int num_blocks, int max_blocks, float scale_log2, int bps,
                    int max_splits, int os_h, int os_d, DecodeWorkspace ws, int* status,
-                   uint64_t wait_limit, int starve) {
+                   uint64_t wait_limit, int starve, const __grid_constant__ NewToken<T> nt) {
   using Cfg = FastCfg<D>;
   constexpr int NS = Cfg::kStages;
   constexpr int KT = D / 16;  // k-steps of QK^T == m-tiles of O^T
@@ -340,6 +432,13 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
   if (warp == Cfg::kConsumerWarps) {
     // ------------------------------ producer ------------------------------
+    // The split holding the sequence's last block writes the new token first (the
+    // other splits never read that slot).
+    if (kNewToken && split == nsplit - 1) {
+      write_new_token<T, D>(nt, b, g, Kh, lane, status);
+      __syncwarp();
+      if (lane == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     // starve != 0 (test hook only): issue nothing, so the consumers' waits run out.
     if (lane == 0 && !starve) {
       tma_prefetch_desc(&tmap_k);
@@ -383,7 +482,10 @@ decode_fast_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
   if (warp < Cfg::kConsumerWarps) {
     uint32_t qb[KT][2];
-    load_q_frags<T, D>(qb, q, q_stride, b, g, group, lane);
+    if (kNewToken)
+      load_q_frags_rope<T, D>(qb, nt, b, g, group, lane);
+    else
+      load_q_frags<T, D>(qb, q, q_stride, b, g, group, lane);
 
     for (int it = 0; it < niter; ++it) {
       const int st = it % NS;
@@ -670,20 +772,31 @@ template <typename T, int D>
 int launch_fast(T* out, const T* q, int64_t q_stride, const void* k_cache, const void* v_cache,
                 const int32_t* bt, int64_t bt_stride, const int32_t* seq_lens_k, int B, int H,
                 int Kh, int num_blocks, int max_blocks, float scale, int bps, int max_splits,
-                int os_h, int os_d, DecodeWorkspace ws, cudaStream_t stream) {
+                int os_h, int os_d, DecodeWorkspace ws, cudaStream_t stream,
+                const NewToken<T>* nt = nullptr) {
   using Cfg = FastCfg<D>;
   CUtensorMap mk, mv;
   int rc = make_pool_map<T>(&mk, k_cache, Kh, D, num_blocks);
   if (rc) return rc;
   rc = make_pool_map<T>(&mv, v_cache, Kh, D, num_blocks);
   if (rc) return rc;
-  auto kern = decode_fast_kernel<T, D>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   dim3 grid(max_splits, Kh, B);
+  const int starve = take_starve_flag(AS_KERNEL_DECODE_ATTENTION) ? 1 : 0;
+  if (nt) {
+    auto kern = decode_fast_kernel<T, D, true>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    launch_pdl(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, mk, mv, out, q,
+               q_stride, bt, bt_stride, seq_lens_k, H, Kh, H / Kh, num_blocks, max_blocks,
+               scale * kLog2e, bps, max_splits, os_h, os_d, ws, device_status_ptr(),
+               wait_limit_ns(), starve, *nt);
+    return check_launch("as_rope_paged_decode_attention");
+  }
+  auto kern = decode_fast_kernel<T, D, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  NewToken<T> none{};
   launch_pdl(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, mk, mv, out, q, q_stride,
              bt, bt_stride, seq_lens_k, H, Kh, H / Kh, num_blocks, max_blocks, scale * kLog2e, bps,
-             max_splits, os_h, os_d, ws, device_status_ptr(), wait_limit_ns(),
-             take_starve_flag(AS_KERNEL_DECODE_ATTENTION) ? 1 : 0);
+             max_splits, os_h, os_d, ws, device_status_ptr(), wait_limit_ns(), starve, none);
   return check_launch("as_paged_decode_attention");
 }
 
@@ -850,6 +963,71 @@ extern "C" int as_paged_decode_attention(void* out, const void* q, int64_t q_str
           k_cache, v_cache, block_tables, bt_stride, seq_lens_k, B, H, Kh, D, num_blocks,
           max_blocks, scale, blocks_per_split, max_splits, os_h, os_d, ws, s);
   }
+}
+
+extern "C" int as_rope_paged_decode_attention(
+    void* out, const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+    int64_t v_stride, const int64_t* positions, const int64_t* slot_mapping,
+    const float* cos_sin, int32_t table_len, void* k_cache, void* v_cache,
+    const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens_k, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t num_blocks, int32_t max_blocks, float scale, int32_t blocks_per_split,
+    void* workspace, size_t workspace_bytes_given, int32_t out_layout, int32_t dtype,
+    as_stream_t stream) {
+  const char* who = "as_rope_paged_decode_attention";
+  const int rc0 = check_decode_args(who, out, q, q_stride, k_cache, v_cache, block_tables,
+                                    bt_stride, seq_lens_k, num_seqs, num_heads, num_kv_heads,
+                                    head_dim, block_size, num_blocks, max_blocks,
+                                    blocks_per_split, out_layout, dtype);
+  if (rc0 != AS_OK) return rc0;
+  if (num_seqs == 0) return AS_OK;
+  if (!k || !v || !positions || !slot_mapping || !cos_sin)
+    return fail(AS_ERR_INVALID_ARG, "%s: null pointer", who);
+  if (table_len <= 0 || k_stride < int64_t(num_kv_heads) * head_dim ||
+      v_stride < int64_t(num_kv_heads) * head_dim)
+    return fail(AS_ERR_INVALID_ARG, "%s: bad table length or k / v row stride", who);
+  const int group = num_heads / num_kv_heads;
+  if (!fast_path_ok(dtype, head_dim, group, q, q_stride, k_cache, v_cache))
+    return fail(AS_ERR_UNSUPPORTED,
+                "%s: needs bf16 / fp16, head_dim 64 or 128, at most 8 query heads per KV head "
+                "and 4-byte aligned rows (use as_rope_reshape_and_cache + "
+                "as_paged_decode_attention)", who);
+  if (blocks_per_split == 0)
+    blocks_per_split = auto_blocks_per_split(num_seqs, num_kv_heads, max_blocks, true);
+  if (blocks_per_split > FastCfg<64>::kMaxBlocksPerSplit)
+    return fail(AS_ERR_INVALID_ARG, "%s: blocks_per_split > %d", who,
+                FastCfg<64>::kMaxBlocksPerSplit);
+  const int max_splits = (max_blocks + blocks_per_split - 1) / blocks_per_split;
+  DecodeWorkspace ws{nullptr, nullptr, nullptr, nullptr};
+  if (max_splits > 1) {
+    const size_t need = workspace_bytes(num_seqs, num_heads, num_heads, head_dim, max_splits);
+    if (!workspace || workspace_bytes_given < need)
+      return fail(AS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed", who, need);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+      return fail(AS_ERR_INVALID_ARG, "%s: workspace must be 256-byte aligned", who);
+    ws = carve_workspace(workspace, num_seqs, num_heads, num_heads, head_dim, max_splits);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int B = num_seqs, H = num_heads, Kh = num_kv_heads, D = head_dim;
+  const int os_h = out_layout == AS_LAYOUT_HEAD_MAJOR ? D : 1;
+  const int os_d = out_layout == AS_LAYOUT_HEAD_MAJOR ? 1 : H;
+  const int64_t num_slots = int64_t(num_blocks) * kBlockSize;
+  auto run = [&](auto tag) -> int {
+    using T = decltype(tag);
+    NewToken<T> nt{static_cast<const T*>(q), q_stride, static_cast<const T*>(k), k_stride,
+                   static_cast<const T*>(v), v_stride, positions, slot_mapping, cos_sin,
+                   table_len, static_cast<T*>(k_cache), static_cast<T*>(v_cache), num_slots};
+    if (D == 64)
+      return launch_fast<T, 64>(static_cast<T*>(out), static_cast<const T*>(q), q_stride,
+                                k_cache, v_cache, block_tables, bt_stride, seq_lens_k, B, H, Kh,
+                                num_blocks, max_blocks, scale, blocks_per_split, max_splits,
+                                os_h, os_d, ws, s, &nt);
+    return launch_fast<T, 128>(static_cast<T*>(out), static_cast<const T*>(q), q_stride, k_cache,
+                               v_cache, block_tables, bt_stride, seq_lens_k, B, H, Kh, num_blocks,
+                               max_blocks, scale, blocks_per_split, max_splits, os_h, os_d, ws, s,
+                               &nt);
+  };
+  return dtype == AS_DTYPE_BF16 ? run(__nv_bfloat16()) : run(__half());
 }
 
 // ===========================================================================

@@ -175,6 +175,10 @@ class B200LlamaModel(nn.Module):
         # measured slower than cuBLAS on B200 at batch 64 (the weight stream's ramp and
         # the on-chip exchange of the K-split partials are the limits).
         self.small_batch_linear: bool = False
+        # True: the paged decode step does the new token's RoPE + cache write inside the
+        # attention launch (as_rope_paged_decode_attention, bf16/fp16, head_dim 64/128);
+        # False: separate RoPE + cache-write launch first (same results, bit for bit)
+        self.fused_rope_decode: bool = True
         self.max_decode_graphs: int = 16
         self._graphs: "OrderedDict[tuple, _PagedStepGraph]" = OrderedDict()
         self._graph_pool = None
@@ -440,6 +444,10 @@ class B200LlamaModel(nn.Module):
         def attention(li, layer, h):
             q, k, v = self._qkv(layer, h)
             kp, vp = allocator.k_plane(li), allocator.v_plane(li)
+            if self.fused_rope_decode and ops.rope_decode_fusable(q, kp):
+                return ops.rope_paged_decode_attention(
+                    q, k, v, pos, pk.slot_mapping, self.rope_table, kp, vp, pk.block_tables,
+                    pk.seq_lens_k, self.scale, bps, ws, out_layout=self.decode_layout)
             ops.rope_reshape_and_cache(q, k, v, pos, pk.slot_mapping, self.rope_table, kp, vp)
             return ops.paged_decode_attention(q, kp, vp, pk.block_tables, pk.seq_lens_k,
                                               self.scale, bps, ws, out_layout=self.decode_layout)

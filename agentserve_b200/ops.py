@@ -241,6 +241,55 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
     return out
 
 
+def rope_decode_fusable(q: torch.Tensor, k_cache: torch.Tensor) -> bool:
+    """True when rope_paged_decode_attention's one-launch path applies (bf16 / fp16,
+    head_dim 64 or 128, at most 8 query heads per KV head)."""
+    B, H, D = q.shape
+    Kh = k_cache.shape[2]
+    return (q.dtype in (torch.bfloat16, torch.float16) and D in (64, 128) and H % Kh == 0
+            and H // Kh <= 8)
+
+
+def rope_paged_decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                positions: torch.Tensor, slot_mapping: torch.Tensor,
+                                cos_sin: torch.Tensor, k_cache: torch.Tensor,
+                                v_cache: torch.Tensor, block_tables: torch.Tensor,
+                                seq_lens_k: torch.Tensor, scale: float, blocks_per_split: int,
+                                workspace: Optional[torch.Tensor],
+                                out: Optional[torch.Tensor] = None,
+                                out_layout: int = N.AS_LAYOUT_HEAD_MAJOR) -> torch.Tensor:
+    """The decode step's RoPE + cache write of the new token and its attention in one
+    launch (as_rope_paged_decode_attention): q [B, H, D], k / v [B, Kh, D] unrotated
+    (row-strided views allowed, left unmodified), positions / slot_mapping [B] int64,
+    cos_sin the fp32 table.  Same results as rope_reshape_and_cache followed by
+    paged_decode_attention; fast path only (rope_decode_fusable)."""
+    _cuda(q, k, v, positions, slot_mapping, cos_sin, k_cache, v_cache, block_tables,
+          seq_lens_k, workspace, out)
+    B, H, D = q.shape
+    NB, bs, Kh, D2 = k_cache.shape
+    _require(bs == BLOCK_SIZE and D2 == D and v_cache.shape == k_cache.shape,
+             "k_cache / v_cache must be [NB, 16, Kh, D] with q's head_dim")
+    _require(k_cache.is_contiguous() and v_cache.is_contiguous(), "KV planes must be contiguous")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require(_row_view_ok(t), f"{name} must be [B, heads, D] with contiguous rows")
+    _require(k.shape == (B, Kh, D) and v.shape == (B, Kh, D), "k / v must be [B, Kh, D]")
+    _require(cos_sin.dtype == torch.float32 and cos_sin.is_contiguous(),
+             "cos_sin must be a contiguous float32 table")
+    _require(block_tables.dtype == torch.int32 and block_tables.stride(1) == 1,
+             "block_tables must be int32 with contiguous rows")
+    if out is None:
+        out = torch.empty(B, H * D, dtype=q.dtype, device=q.device)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    N.check(N.load().as_rope_paged_decode_attention(
+        _ptr(out), _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
+        _ptr(positions), _ptr(slot_mapping), _ptr(cos_sin), cos_sin.shape[0], _ptr(k_cache),
+        _ptr(v_cache), _ptr(block_tables), block_tables.stride(0), _ptr(seq_lens_k), B, H, Kh, D,
+        BLOCK_SIZE, NB, block_tables.shape[1], float(scale), int(blocks_per_split),
+        _ptr(workspace), ws_bytes, int(out_layout), dtype_code(q.dtype), _stream(q.device)),
+        "as_rope_paged_decode_attention")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # (4) varlen prefill attention
 # ---------------------------------------------------------------------------

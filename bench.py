@@ -952,9 +952,11 @@ def run_b200(args):
                     # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
                     # the greedy int64 tokens out
                     "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8},
-            # per step: pack + first RMSNorm + greedy argmax + per layer (RoPE/cache,
-            # attention, 2 x add+RMSNorm, SwiGLU); the projections and lm_head are cuBLAS
-            "gpu_launches": args.steps * (3 + 5 * cfg.n_layers),
+            # per step: pack + first RMSNorm + greedy argmax + per layer (RoPE/cache +
+            # attention in one launch, or two, 2 x add+RMSNorm, SwiGLU); the projections
+            # and lm_head are cuBLAS
+            "gpu_launches": args.steps * (3 + (4 if model.fused_rope_decode else 5)
+                                          * cfg.n_layers),
             "per_rank": per_rank,
             "strong": strong,
             "config5": c5,

@@ -22,6 +22,8 @@
  *                             (write_kv_prefill / write_kv_decode)
  *   as_paged_decode_attention llama.py:419-469 (gather_kv -> pad -> GQA expand -> SDPA)
  *                             and llama.py:303-361 (padded-list decode)
+ *   as_rope_paged_decode_attention  llama.py:433-469 (RoPE of the new token, its
+ *                             write_kv_decode and the attention) in one launch
  *   as_varlen_prefill_attention llama.py:128-186 (prefill over cached prefix + new tokens)
  *   as_varlen_prefill_attention_ws  the same, split-KV over CTAs with a workspace
  *   as_linear_small_m         nn.Linear of the decode step (llama.py:123-126, 203-211,
@@ -180,6 +182,29 @@ AS_API int as_paged_decode_attention(void* out, const void* q, int64_t q_stride,
                               float scale, int32_t blocks_per_split, void* workspace,
                               size_t workspace_bytes, int32_t out_layout, int32_t dtype,
                               as_stream_t stream);
+
+/* The decode step's RoPE + cache write and its attention in one launch: replaces
+ * apply_rope on the new token's q and k (llama.py:433-434), write_kv_decode
+ * (llama.py:437-439, cache.py:142-156) and the attention (llama.py:441-469).  q, k, v
+ * are the new token's UNROTATED projections ([B, H, D] / [B, Kh, D] rows, strides in
+ * elements, e.g. column slices of a fused QKV output; none is modified); positions /
+ * slot_mapping [B] int64 as for as_rope_reshape_and_cache (a bad position or slot is
+ * flagged and skipped the same way).  The CTA that reads a sequence's last block
+ * writes the rotated k and v into the pool first; q is rotated as it is loaded.  The
+ * pool bytes and the output equal those of as_rope_reshape_and_cache followed by
+ * as_paged_decode_attention bit for bit.  Fast path only (bf16 / fp16, head_dim 64 or
+ * 128, GQA group <= 8); otherwise AS_ERR_UNSUPPORTED, and the two calls above apply.
+ * Other arguments as as_paged_decode_attention (seq_lens_k counts the new token). */
+AS_API int as_rope_paged_decode_attention(void* out, const void* q, int64_t q_stride, const void* k,
+                              int64_t k_stride, const void* v, int64_t v_stride,
+                              const int64_t* positions, const int64_t* slot_mapping,
+                              const float* cos_sin, int32_t table_len, void* k_cache,
+                              void* v_cache, const int32_t* block_tables, int64_t bt_stride,
+                              const int32_t* seq_lens_k, int32_t num_seqs, int32_t num_heads,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int32_t num_blocks, int32_t max_blocks, float scale,
+                              int32_t blocks_per_split, void* workspace, size_t workspace_bytes,
+                              int32_t out_layout, int32_t dtype, as_stream_t stream);
 
 /* Same computation as as_paged_decode_attention, for callers that cannot allocate
  * device memory (their GPU memory belongs to another allocator, or their serving loop

@@ -602,3 +602,56 @@ def test_ops_reject_bad_layouts_with_value_error():
         ops.linear_small_m(xb, torch.randn(256, 128, device=DEV, dtype=torch.bfloat16),
                            out=torch.empty(8, 128, device=DEV, dtype=torch.bfloat16))
     status_ok()
+
+
+# ---------------------------------------------------------------- fused RoPE + decode
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bps", [0, 4])
+def test_rope_decode_one_launch_equals_two_launches(dtype, D, bps):
+    """as_rope_paged_decode_attention (the new token's RoPE + cache write inside the
+    attention launch) leaves the same pool bytes and returns the same output, bit for
+    bit, as as_rope_reshape_and_cache followed by as_paged_decode_attention; q, k, v
+    are strided column slices of one fused projection output, as in the decode step;
+    one slot is negative (skipped) and the output is also checked against the oracle."""
+    H, Kh = 32, 8
+    g = torch.Generator().manual_seed(D + bps)
+    hist = [0, 15, 16, 100, 1000, 2111, 4095, 31]
+    lens_k = [L + 1 for L in hist]
+    NB = sum((L + 15) // 16 for L in lens_k) + 8
+    tables = make_tables(lens_k, NB, g)
+    kp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype).to(DEV)
+    vp = torch.randn(NB, 16, Kh, D, generator=g).to(dtype).to(DEV)
+    B = len(hist)
+    qkv = torch.randn(B, (H + 2 * Kh) * D, generator=g).to(dtype).to(DEV)
+    table = OR.precompute_rope_freqs(D, 8192, 500000.0).to(DEV)
+    pos = torch.tensor(hist, dtype=torch.int64, device=DEV)
+    slots = [t[L // 16] * 16 + L % 16 for t, L in zip(tables, hist)]
+    slots[3] = -1  # written by neither path
+    slot_t = torch.tensor(slots, dtype=torch.int64, device=DEV)
+    bt = padded(tables).to(DEV)
+    lk = torch.tensor(lens_k, dtype=torch.int32, device=DEV)
+
+    def split(x):
+        return (x[:, :H * D].view(B, H, D), x[:, H * D:(H + Kh) * D].view(B, Kh, D),
+                x[:, (H + Kh) * D:].view(B, Kh, D))
+
+    ws = ops.new_decode_workspace(B, H, Kh, D, bt.shape[1], bps, DEV)
+    kp1, vp1, x1 = kp.clone(), vp.clone(), qkv.clone()
+    q, k, v = split(x1)
+    ops.rope_reshape_and_cache(q, k, v, pos, slot_t, table, kp1, vp1)
+    o1 = ops.paged_decode_attention(q, kp1, vp1, bt, lk, D ** -0.5, bps, ws,
+                                    out_layout=N.AS_LAYOUT_DIM_MAJOR)
+    kp2, vp2, x2 = kp.clone(), vp.clone(), qkv.clone()
+    q, k, v = split(x2)
+    o2 = ops.rope_paged_decode_attention(q, k, v, pos, slot_t, table, kp2, vp2, bt, lk,
+                                         D ** -0.5, bps, ws, out_layout=N.AS_LAYOUT_DIM_MAJOR)
+    torch.cuda.synchronize()
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    assert torch.equal(o1, o2)
+    assert torch.equal(x2, qkv)  # the projections are left as they were
+    ref = OA.flatten_decode_output(OA.decode_attention_from_pool(
+        x1[:, :H * D].view(B, H, D).float().cpu(), kp1.float().cpu(), vp1.float().cpu(), tables,
+        lens_k))
+    torch.testing.assert_close(o2.float().cpu(), ref, rtol=0, atol=ATOL_LOWP)
+    status_ok()
