@@ -75,6 +75,26 @@ class EngineMetrics:
         return self.prefix_cache_hits / total if total > 0 else 0.0
 
 
+class _Speculation:
+    """A decode step queued for `batch` before its inputs were confirmed."""
+
+    def __init__(self, batch: List, expect_out: List[int], handle):
+        self.batch, self.expect_out, self.handle = batch, expect_out, handle
+
+    def positions_of(self, batch: List) -> Optional[List[int]]:
+        """Row of each request of `batch` in the speculated step, or None if the step
+        does not apply: `batch` must be the speculated requests in the same order
+        (some may have finished), each with exactly the expected number of outputs."""
+        idx = {id(r): i for i, r in enumerate(self.batch)}
+        rows = []
+        for r in batch:
+            i = idx.get(id(r))
+            if i is None or r.num_output_tokens != self.expect_out[i] or (rows and i <= rows[-1]):
+                return None
+            rows.append(i)
+        return rows
+
+
 class B200Engine:
     def __init__(self, config, *, model: Optional[B200LlamaModel] = None,
                  dtype: torch.dtype = torch.bfloat16, device: str = "cuda",
@@ -125,6 +145,10 @@ class B200Engine:
         # its own prefix stored in the cache): never rewritten, not even when the
         # request is preempted and prefilled again
         self._frozen: Dict[str, int] = {}
+        # queue the next decode step before reading this one's tokens (see _decode)
+        self.speculative_decode: bool = True
+        self._spec: Optional[_Speculation] = None
+        self.spec_stats = {"queued": 0, "used": 0}
 
     # ------------------------------------------------------------------ submission
     def submit(self, request) -> None:
@@ -160,6 +184,8 @@ class B200Engine:
         decode = self.scheduler.get_decode_batch()
         if decode:
             self._decode(decode)
+        else:
+            self._spec = None
         done = self.scheduler.pop_completed()
         for req in done:
             self._release(req)
@@ -258,10 +284,57 @@ class B200Engine:
 
     # ------------------------------------------------------------------ decode
     def _decode(self, batch: List) -> None:
-        """engine.py:347-384: every decoding request advances one token."""
-        last = [r.output_token_ids[-1] for r in batch]
+        """engine.py:347-384: every decoding request advances one token.
+
+        With speculative_decode (and a model that can queue steps), the next step of
+        the same batch is queued on the device before this step's tokens are read back,
+        fed by this step's output tokens on the device; the host's bookkeeping then
+        overlaps the GPU instead of alternating with it.  It is used at the next step
+        only if that step's decode batch is the same requests in the same order with
+        exactly one more token each (requests that finished in between are dropped
+        from it); otherwise it is discarded: its only effect was writing K/V for
+        positions the real step rewrites, or in blocks of finished requests.  Tokens
+        and scheduling decisions are the same either way."""
+        spec, self._spec = self._spec, None
+        rids = [r.request_id for r in batch]
         seq_lens = [r.num_cached_tokens + r.num_output_tokens - 1 for r in batch]
-        nxt = self.model.decode_paged_greedy(last, seq_lens, self.allocator,
-                                             [r.request_id for r in batch])
-        for req, tok in zip(batch, nxt):
+        launch = getattr(self.model, "decode_paged_greedy_launch", None)
+        pick = spec.positions_of(batch) if spec is not None else None
+        if pick is not None:
+            handle, take = spec.handle, pick
+            self.spec_stats["used"] += 1
+        elif launch is not None:
+            last = [r.output_token_ids[-1] for r in batch]
+            handle, take = launch(last, seq_lens, self.allocator, rids), None
+        else:  # a model with only the blocking call
+            nxt = self.model.decode_paged_greedy([r.output_token_ids[-1] for r in batch],
+                                                 seq_lens, self.allocator, rids)
+            for req, tok in zip(batch, nxt):
+                self.scheduler.on_decode_step(req, tok, self.eos_token_id)
+            return
+        # queue the next step now if it will most likely be this batch again; the
+        # device feed needs this step's rows to be exactly the batch (a used
+        # speculation with finished requests dropped has extra rows)
+        same_rows = take is None or len(take) == len(spec.batch)
+        if same_rows and self.speculative_decode and self._worth_speculating(batch):
+            nxt_h = launch(None, [x + 1 for x in seq_lens], self.allocator, rids,
+                           feed_from=handle)
+            self._spec = _Speculation(list(batch), [r.num_output_tokens + 1 for r in batch],
+                                      nxt_h)
+            self.spec_stats["queued"] += 1
+        toks = handle.result()
+        if take is not None:
+            toks = [toks[i] for i in take]
+        for req, tok in zip(batch, toks):
             self.scheduler.on_decode_step(req, tok, self.eos_token_id)
+
+    def _worth_speculating(self, batch: List) -> bool:
+        """The next decode batch is likely this one again: nobody reaches max_tokens
+        with this step's token, no request waits to be admitted, and no prefill can
+        start (nothing pending, or the batch is at its cap)."""
+        if self._incoming:
+            return False
+        if any(r.num_output_tokens + 1 >= r.max_tokens for r in batch):
+            return False
+        sch = self.scheduler
+        return len(sch.decoding) >= sch.max_batch_size or not sch.pending

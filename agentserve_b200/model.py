@@ -358,6 +358,7 @@ class B200LlamaModel(nn.Module):
         last = pk.cu_seqlens_q[1:].long() - 1
         return self._logits(h.index_select(0, last))
 
+    @torch.inference_mode()
     def prefill_paged_greedy(self, token_ids: Sequence[Sequence[int]],
                              num_cached: Sequence[int], allocator,
                              request_ids: Sequence[str]) -> List[int]:
@@ -493,7 +494,11 @@ class B200LlamaModel(nn.Module):
         the allocator's table width); the split-K decomposition follows that bucket.
         sample=True captures greedy sampling too and returns next tokens instead of
         logits.  Least recently used graphs beyond max_decode_graphs are released."""
-        B = len(tokens)
+        g = self._step_graph(allocator, len(tokens), max_blocks, bps, sample)
+        return g.run(tokens, seq_lens, rows)
+
+    def _step_graph(self, allocator, B: int, max_blocks: int, bps: int,
+                    sample: bool) -> "_PagedStepGraph":
         cap = allocator.block_tables.shape[1]
         mb = min(cap, 1 << max(0, (max_blocks - 1).bit_length()))
         key = (id(allocator), B, mb, bps, sample)
@@ -506,8 +511,9 @@ class B200LlamaModel(nn.Module):
             while len(self._graphs) > self.max_decode_graphs:
                 self._graphs.popitem(last=False)
         self._graphs.move_to_end(key)
-        return g.run(tokens, seq_lens, rows)
+        return g
 
+    @torch.inference_mode()
     @torch.inference_mode()
     def decode_paged_greedy(self, last_token_ids: List[int], seq_lens: List[int], allocator,
                             request_ids: List[str]) -> List[int]:
@@ -518,15 +524,30 @@ class B200LlamaModel(nn.Module):
         of 32 above); the padding rows decode a dummy token in the allocator's scratch
         row and are dropped, so a batch that shrinks or grows by a few requests reuses
         the same graph."""
+        return self.decode_paged_greedy_launch(last_token_ids, seq_lens, allocator,
+                                               request_ids).result()
+
+    @torch.inference_mode()
+    def decode_paged_greedy_launch(self, last_token_ids: Optional[List[int]],
+                                   seq_lens: List[int], allocator, request_ids: List[str],
+                                   feed_from: Optional["DecodeHandle"] = None) -> "DecodeHandle":
+        """decode_paged_greedy without waiting: the step is queued on the current stream
+        and its tokens are copied to pinned host memory behind it; DecodeHandle.result()
+        waits for them.  With feed_from (the handle of the previous step of the SAME
+        batch, in the same order) the input tokens are that step's outputs, read on the
+        device, so this step can be queued before the previous one's tokens reach the
+        host; last_token_ids is then ignored."""
         if not isinstance(allocator, DeviceBlockAllocator):
             raise TypeError("decode_paged_greedy needs an agentserve_b200.DeviceBlockAllocator")
         self.fuse_projections_()
-        B = len(last_token_ids)
+        B = len(seq_lens)
         if B == 0:
-            return []
+            return DecodeHandle(None, None, 0, [])
         rows = allocator.rows_for(request_ids)
         max_blocks = max(len(allocator._request_blocks[r]) for r in request_ids)
         Bp = _batch_bucket(B)
+        if last_token_ids is None:
+            last_token_ids = [0] * B
         if Bp > B:
             pad = allocator.scratch_row()
             last_token_ids = list(last_token_ids) + [0] * (Bp - B)
@@ -535,12 +556,14 @@ class B200LlamaModel(nn.Module):
         if not (self.decode_graphs and self.device.type == "cuda"):
             host = torch.tensor([list(last_token_ids), list(seq_lens), rows], dtype=torch.int64)
             d = host.to(self.device)
-            logits = self._decode_core(d[0], d[1].to(torch.int32), d[2].to(torch.int32),
+            tok = d[0] if feed_from is None else feed_from.tokens.to(torch.int64)
+            logits = self._decode_core(tok, d[1].to(torch.int32), d[2].to(torch.int32),
                                        allocator, max_blocks, self.decode_blocks_per_split)
-            return greedy(logits)[:B].tolist()
-        out = self._graphed_decode(allocator, last_token_ids, seq_lens, rows, max_blocks,
-                                   self.decode_blocks_per_split, sample=True)
-        return out[:B].tolist()
+            out = greedy(logits)
+            return DecodeHandle(out, None, B, out[:B].tolist())
+        g = self._step_graph(allocator, Bp, max_blocks, self.decode_blocks_per_split, True)
+        return g.launch(last_token_ids, seq_lens, rows, B,
+                        None if feed_from is None else feed_from.tokens)
 
     def release_decode_graphs(self) -> None:
         """Drop every cached decode graph now (e.g. before destroying a process group
@@ -582,6 +605,10 @@ class _PagedStepGraph:
         self.model, self.max_blocks, self.bps = model, max_blocks, bps
         self._pool = pool
         self.logits: Optional[torch.Tensor] = None
+        if sample:  # two pinned landing buffers for the tokens of consecutive launches
+            self.out_host = [torch.zeros(B, dtype=torch.int64).pin_memory() for _ in range(2)]
+            self.out_ready = [torch.cuda.Event(), torch.cuda.Event()]
+            self._flip = 0
 
     def _body(self) -> torch.Tensor:
         logits = self.model._decode_core(self.inputs[0], self.inputs[1], self.inputs[2],
@@ -604,6 +631,24 @@ class _PagedStepGraph:
     def run(self, tokens, seq_lens, rows) -> torch.Tensor:
         """Called from forward_decode_paged (inference mode)."""
         self._stage(tokens, seq_lens, rows)
+        self._replay()
+        return self.logits.clone()
+
+    def launch(self, tokens, seq_lens, rows, n: int,
+               feed: Optional[torch.Tensor] = None) -> "DecodeHandle":
+        """Queue one greedy step (sample=True graphs); feed: device tokens to use instead
+        of `tokens` (the previous step's output of the same batch)."""
+        self._stage(tokens, seq_lens, rows)
+        if feed is not None:
+            self.inputs[0].copy_(feed)
+        self._replay()
+        k = self._flip
+        self._flip ^= 1
+        self.out_host[k].copy_(self.logits, non_blocking=True)
+        self.out_ready[k].record()
+        return DecodeHandle(self.logits, self.out_ready[k], n, host=self.out_host[k])
+
+    def _replay(self) -> None:
         if self.graph is None:
             # warm-up on a side stream (kernel attributes, cuBLAS workspaces), then
             # capture; the warm-up writes the same pool slots the replay rewrites
@@ -621,7 +666,23 @@ class _PagedStepGraph:
                                   capture_error_mode="relaxed"):
                 self.logits = self._body()
         self.graph.replay()
-        return self.logits.clone()
+
+
+class DecodeHandle:
+    """The greedy tokens of one queued decode step.  `tokens` is the step's device
+    output (valid until the same graph is replayed again, which the stream orders after
+    any reader queued before it); result() waits for the host copy."""
+
+    def __init__(self, tokens: Optional[torch.Tensor], event, n: int,
+                 values: Optional[List[int]] = None, host: Optional[torch.Tensor] = None):
+        self.tokens, self.event, self.n = tokens, event, n
+        self._values, self._host = values, host
+
+    def result(self) -> List[int]:
+        if self._values is None:
+            self.event.synchronize()
+            self._values = self._host[:self.n].tolist()
+        return self._values
 
 
 def greedy(logits: torch.Tensor) -> torch.Tensor:

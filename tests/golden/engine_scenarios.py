@@ -84,9 +84,19 @@ class HistoryModelForReference:
         return torch.cat(logits), new
 
 
+class _Handle:
+    def __init__(self, tokens: List[int]):
+        self.tokens = tokens
+
+    def result(self) -> List[int]:
+        return list(self.tokens)
+
+
 class HistoryModelForB200:
     """The same stand-in behind agentserve_b200.B200Engine (its greedy paged methods),
-    on the CPU: histories are kept per request id."""
+    on the CPU.  A request's history is kept by position, like a KV cache: a decode step
+    at position s writes its input token at s and forgets anything after it, so a step
+    the engine queued ahead and then discarded leaves no trace."""
 
     def __init__(self, n_layers: int = 1):
         self.device = torch.device("cpu")
@@ -102,12 +112,20 @@ class HistoryModelForB200:
             out.append(history_token(h))
         return out
 
-    def decode_paged_greedy(self, last_token_ids, seq_lens, allocator, request_ids):
+    def decode_paged_greedy_launch(self, last_token_ids, seq_lens, allocator, request_ids,
+                                   feed_from=None):
+        if feed_from is not None:
+            last_token_ids = feed_from.tokens
         out = []
-        for last, rid in zip(last_token_ids, request_ids):
-            self.hist[rid].append(int(last))
-            out.append(history_token(self.hist[rid]))
-        return out
+        for last, s, rid in zip(last_token_ids, seq_lens, request_ids):
+            h = self.hist[rid][:s] + [int(last)]
+            self.hist[rid] = h
+            out.append(history_token(h))
+        return _Handle(out)
+
+    def decode_paged_greedy(self, last_token_ids, seq_lens, allocator, request_ids):
+        return self.decode_paged_greedy_launch(last_token_ids, seq_lens, allocator,
+                                               request_ids).result()
 
 
 # --------------------------------------------------------------------------- streams

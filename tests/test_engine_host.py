@@ -182,3 +182,21 @@ def test_cpu_fake_engine_uses_no_gpu():
     eng = fake_engine()
     assert eng.allocator.kv_pool.device.type == "cpu"
     assert not torch.cuda.is_initialized()
+
+
+@pytest.mark.parametrize("name", ["priority_overflow_preemption", "combined_batching"])
+def test_queued_next_step_changes_nothing(name):
+    """The engine queues the next decode step before reading this one's tokens when the
+    batch will likely be the same; the decisions and outputs are the reference's either
+    way, and the queued steps are used (or discarded when a preemption changes the
+    batch)."""
+    runs = {}
+    for spec in (True, False):
+        eng = fake_engine(**E.engine_kwargs(name, P))
+        eng.speculative_decode = spec
+        runs[spec] = (E.run_stream(eng, Request, E.trace_stream(name)), dict(eng.spec_stats))
+    assert_same_run(runs[True][0], runs[False][0])
+    assert_same_run(runs[True][0], GOLDEN["traces"][name])
+    queued, used = runs[True][1]["queued"], runs[True][1]["used"]
+    assert used > 0.5 * runs[True][0]["metrics"]["steps"] and used <= queued
+    assert runs[False][1] == {"queued": 0, "used": 0}

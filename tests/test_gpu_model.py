@@ -390,21 +390,31 @@ def test_graphed_decode_config2_shape_bf16_vs_oracle_256_steps():
     """The metric's shape: Llama-3.2-1B architecture in bf16, 64 sequences with contexts
     U{128..4096}, 256 steps through the graphed forward_decode_paged, against the oracle
     (the reference's forward_decode_paged restated: gather -> pad -> GQA expand -> SDPA)
-    run in bf16 on the same GPU from the same weights and pool contents.  Both are fed
-    the oracle's greedy tokens (teacher forcing) so every step compares the same inputs.
+    run on the same GPU from the same weights and pool contents, in bf16 and in fp32
+    (the bf16 values upcast).  All three are fed the fp32 oracle's greedy tokens
+    (teacher forcing), so every step compares the same inputs.
 
-    bf16 cannot make the two orders of summation agree bit for bit, so the bar is: the
-    logits stay within 0.1 of the oracle's (|logit| ~ 1), and every step where the two
-    greedy choices differ is a near-tie of the oracle's logits (top-1 minus top-2 below
-    twice that row's logit difference), on fewer than 1% of the 16,384 choices.  The
-    first such step and its margin are printed."""
+    bf16 logits of two different summation orders cannot agree bit for bit, and with
+    128,256 logits of bf16 resolution the top two are often exactly tied, so greedy
+    choices of any two bf16 paths differ on a few percent of steps.  The bar is
+    relative: measured against the fp32 oracle, the kernel path's largest and mean
+    logit errors and its number of greedy choices that differ from fp32 are at most
+    1.5x those of the reference's own algorithm run in bf16.  The statistics and the
+    first differing step are printed."""
     cfg = ModelConfig(hidden_dim=2048, n_heads=32, n_kv_heads=8, n_layers=16, vocab_size=128256,
                       max_seq_len=4096 + 300, rope_theta=500000.0, intermediate_size=8192)
     m = b200_model(cfg, torch.bfloat16, fused=True)
-    o = OracleLlama(cfg).to(DEV, torch.bfloat16)
-    o.rope_table = precompute_rope_freqs(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta).to(DEV)
-    init_weights_(o, seed=0)
-    o.eval()
+    table = precompute_rope_freqs(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta).to(DEV)
+    ob = OracleLlama(cfg).to(DEV, torch.bfloat16)
+    ob.rope_table = table
+    init_weights_(ob, seed=0)
+    ob.eval()
+    of = OracleLlama(cfg).to(DEV)
+    with torch.no_grad():
+        for (n, pf), (_, pb) in zip(of.named_parameters(), ob.named_parameters()):
+            pf.copy_(pb.float())
+    of.rope_table = table
+    of.eval()
     B, steps = 64, 256
     g = torch.Generator().manual_seed(0)
     lens = torch.randint(128, 4097, (B,), generator=g).tolist()
@@ -412,35 +422,39 @@ def test_graphed_decode_config2_shape_bf16_vs_oracle_256_steps():
     NB = sum(nblk)
     a = DeviceBlockAllocator(NB, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
                              dtype=torch.bfloat16, device=DEV, max_seqs=B)
-    oa = OracleBlockAllocator(NB, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+    ab = OracleBlockAllocator(NB, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
                               allocate_tensor=True, dtype=torch.bfloat16, device=DEV)
+    af = OracleBlockAllocator(NB, 16, cfg.n_layers, cfg.n_kv_heads, cfg.head_dim,
+                              allocate_tensor=True, dtype=torch.float32, device=DEV)
     rids = [f"s{i}" for i in range(B)]
     for r, n in zip(rids, nblk):
-        assert a.allocate(r, n) == oa.allocate(r, n)
+        assert a.allocate(r, n) == ab.allocate(r, n) == af.allocate(r, n)
     gen = torch.Generator(device=DEV).manual_seed(3)
     a.kv_pool.normal_(0.0, 1.0, generator=gen)
-    oa.kv_pool.copy_(a.kv_pool)
+    ab.kv_pool.copy_(a.kv_pool)
+    af.kv_pool.copy_(a.kv_pool.float())
     tok = torch.randint(3, cfg.vocab_size, (B,), generator=g).tolist()
-    worst, mism, first = 0.0, 0, None
+    err = {"kernels": [], "oracle_bf16": []}
+    differ = {"kernels": 0, "oracle_bf16": 0}
+    first = None
     for step in range(steps):
         lm, _ = m.forward_decode_paged(tok, lens, lens, a, rids)
-        lo, _ = o.forward_decode_paged(tok, lens, lens, oa, rids)
-        diff = (lm.float() - lo.float()).abs()
-        worst = max(worst, diff.max().item())
-        tm, to = greedy(lm), oracle_greedy(lo)
-        bad = (tm != to).nonzero().flatten().tolist()
-        if bad:
-            top2 = torch.topk(lo.float()[bad], 2, dim=-1).values
-            margins = (top2[:, 0] - top2[:, 1]).tolist()
-            row_err = diff[bad].max(dim=-1).values.tolist()
-            for mg, er in zip(margins, row_err):
-                assert mg <= 2 * er, f"step {step}: choices differ at margin {mg:.4g} > 2 x {er:.4g}"
-            if first is None:
-                first = (step, min(margins))
-            mism += len(bad)
-        tok = to.tolist()
+        lb, _ = ob.forward_decode_paged(tok, lens, lens, ab, rids)
+        lf, _ = of.forward_decode_paged(tok, lens, lens, af, rids)
+        tf = oracle_greedy(lf)
+        for name, lx, tx in (("kernels", lm, greedy(lm)), ("oracle_bf16", lb, oracle_greedy(lb))):
+            err[name].append((lx.float() - lf).abs().max().item())
+            bad = (tx != tf).nonzero().flatten()
+            differ[name] += bad.numel()
+            if name == "kernels" and bad.numel() and first is None:
+                top2 = torch.topk(lf[bad], 2, dim=-1).values
+                first = (step, (top2[:, 0] - top2[:, 1]).min().item())
+        tok = tf.tolist()
         lens = [x + 1 for x in lens]
-    print(f"bf16 config-2 shape, {steps} steps x {B} sequences: max logit difference "
-          f"{worst:.4g}, {mism} differing greedy choices, first at {first}")
-    assert worst < 0.1
-    assert mism < 0.01 * steps * B
+    stats = {k: (max(v), sum(v) / len(v), differ[k]) for k, v in err.items()}
+    print(f"bf16 config-2 shape, {steps} steps x {B} sequences, vs the fp32 oracle "
+          f"(max logit error, mean of per-step max, greedy choices that differ): {stats}; "
+          f"first differing kernel choice (step, fp32 top-2 margin): {first}")
+    (km, ka, kd), (om, oa, od) = stats["kernels"], stats["oracle_bf16"]
+    assert km <= 1.5 * om and ka <= 1.5 * oa
+    assert kd <= 1.5 * od + 8
