@@ -118,6 +118,10 @@ class B200Engine:
                                                                     device=device)
         self.device = self.model.device
         dtype = self.model.dtype
+        # decode batches come in many (batch size, block bucket) shapes: keep their
+        # captured graphs instead of recapturing as the batch grows and shrinks
+        if hasattr(self.model, "max_decode_graphs"):
+            self.model.max_decode_graphs = max(self.model.max_decode_graphs, 64)
         self.scheduler = scheduler if scheduler is not None else Scheduler(
             max_batch_size=max_batch_size, max_prefill_per_step=max_prefill_per_step,
             baseline_mode=not agent_aware, enable_priority=enable_priority,
