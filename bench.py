@@ -556,6 +556,46 @@ def engine_mixed(args, dev, model):
     return res
 
 
+def engine_decode(args, dev, model, steps: int, warmup: int):
+    """The decode workload through B200Engine.step: the 64 sequences (contexts
+    U{128..4096}, random token ids) are admitted and prefilled by the engine (untimed),
+    then `warmup` and `steps` engine steps decode all 64 at once, each step ending with
+    its tokens on the host (the engine queues the next step on the device before it
+    reads them)."""
+    import numpy as np
+    from agentserve_b200 import B200Engine, Request
+    lens = context_lengths(args.batch, args.ctx_min, args.ctx_max, seed=0)
+    rng = np.random.default_rng(3)
+    n_out = warmup + steps + 32  # nobody finishes inside the timed steps
+    reqs = [Request(prompt="medium 100 decode", token_ids=rng.integers(3, 128000, L).tolist(),
+                    max_tokens=n_out, request_id=f"d{i}") for i, L in enumerate(lens)]
+    blocks = sum(-(-(L + n_out) // 16) for L in lens) + 64
+    eng = B200Engine(model.config, model=model, max_batch_size=args.batch,
+                     max_prefill_per_step=16, num_cache_blocks=blocks, eos_token_id=-1,
+                     max_seqs=args.batch + 8, max_blocks_per_seq=-(-(max(lens) + n_out) // 16))
+    eng.submit_many(reqs)
+    while len(eng.scheduler.decoding) < len(reqs):
+        eng.step()
+    for _ in range(warmup):
+        eng.step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out0 = sum(r.num_output_tokens for r in reqs)
+    for _ in range(steps):
+        eng.step()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    made = sum(r.num_output_tokens for r in reqs) - out0
+    res = {"value": made / wall, "unit": "tok/s", "steps": steps, "sequences": len(reqs),
+           "ms_per_step": wall / steps * 1e3,
+           "queued_decode_steps": dict(eng.spec_stats),
+           "api": "B200Engine.step (scheduler, bookkeeping, one pinned copy of positions "
+                  "and table rows in, the tokens out, every step)"}
+    model.release_decode_graphs()
+    del eng
+    return res
+
+
 def _session_plan(seed: int, sessions: int, turns: int):
     import numpy as np
     rng = np.random.default_rng(seed)
@@ -891,6 +931,18 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _optional(name: str, fn):
+    """Run one of the line's supplementary measurements; a failure there is reported in
+    its place (and on stderr) instead of losing the headline line."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        import traceback
+        traceback.print_exc()
+        print(f"{name} failed: {e!r}", file=sys.stderr, flush=True)
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
 def run_b200(args):
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
@@ -937,47 +989,56 @@ def run_b200(args):
     torch.cuda.empty_cache()
 
     # ---------------- the same 64 sequences split over the N GPUs (strong scaling)
-    strong = None
-    if world > 1 and tp == 1 and not args.no_strong:
+    def strong_scaling():
         all_lens = context_lengths(args.batch, args.ctx_min, args.ctx_max, seed=0)
         mine = all_lens[rank::world]
         srun = DecodeRun(model, mine, args.warmup + args.steps + 4, args.blocks_per_split,
                          seed=900 + rank)
         s_ms = srun.timed_steps(ranks, args.steps, args.warmup)
         s_max = ranks.max(s_ms)
-        strong = {"sequences_total": args.batch, "sequences_per_gpu": len(mine),
-                  "value": args.batch * args.steps / (s_max / 1e3), "unit": "tok/s",
-                  "ms_per_step": s_max / args.steps,
-                  "per_rank_ms_per_step": [x / args.steps for x in ranks.gather(s_ms)],
-                  "note": "strong scaling: total work fixed at the 64 sequences of one GPU's "
-                          "workload, split round-robin over the N GPUs"}
+        res = {"sequences_total": args.batch, "sequences_per_gpu": len(mine),
+               "value": args.batch * args.steps / (s_max / 1e3), "unit": "tok/s",
+               "ms_per_step": s_max / args.steps,
+               "per_rank_ms_per_step": [x / args.steps for x in ranks.gather(s_ms)],
+               "note": "strong scaling: total work fixed at the 64 sequences of one GPU's "
+                       "workload, split round-robin over the N GPUs"}
         srun.free()
-        del srun
         model.release_decode_graphs()
         gc.collect()
         torch.cuda.empty_cache()
+        return res
+
+    strong = None
+    if world > 1 and tp == 1 and not args.no_strong:
+        strong = _optional("strong", strong_scaling)
 
     # ---------------- 8B geometry: replicas, and KV-head TP over the N GPUs
     c5 = None
     if args.model == "1b" and tp == 1 and not args.no_config5:
-        c5 = config5(args, dev, ranks, rank, world)
+        c5 = _optional("config5", lambda: config5(args, dev, ranks, rank, world))
         bits |= ops.device_status(clear=True)
 
     pf = pf128 = c1 = engines = None
     if rank == 0 and world == 1 and tp == 1:
         if not args.no_prefill:
-            pf = measure_prefill(dev)
-            pf128 = measure_prefill(dev, D=128)
+            pf = _optional("prefill", lambda: {"64": measure_prefill(dev),
+                                               "128": measure_prefill(dev, D=128)})
+            if "error" not in pf:
+                pf, pf128 = pf["64"], pf["128"]
+            else:
+                pf = None
         if not args.no_config1:
-            c1 = {"cpu": config1_cpu(), "gpu": config1_gpu(dev),
-                  "case": "one paged decode-attention op: 8 sequences, cached lengths "
-                          "U{17..1024} (seed 0), 512-block pool, 32/8 heads, head_dim 64, "
-                          "fp32; the GPU also at batch 64 / 256 and in bf16"}
+            c1 = _optional("config1", lambda: {
+                "cpu": config1_cpu(), "gpu": config1_gpu(dev),
+                "case": "one paged decode-attention op: 8 sequences, cached lengths "
+                        "U{17..1024} (seed 0), 512-block pool, 32/8 heads, head_dim 64, "
+                        "fp32; the GPU also at batch 64 / 256 and in bf16"})
         if not args.no_engine and args.model == "1b":
-            engines = {"mixed_requests": engine_mixed(args, dev, model),
-                       "prefix_cache_sessions": engine_prefix(args, dev, model,
-                                                              args.engine_sessions,
-                                                              args.engine_turns)}
+            engines = {"decode_through_engine": _optional("engine", lambda: engine_decode(
+                           args, dev, model, max(args.steps, 20), max(args.warmup, 3))),
+                       "mixed_requests": _optional("engine", lambda: engine_mixed(args, dev, model)),
+                       "prefix_cache_sessions": _optional("engine", lambda: engine_prefix(
+                           args, dev, model, args.engine_sessions, args.engine_turns))}
         bits |= ops.device_status(clear=True)
 
     ranks.barrier()
