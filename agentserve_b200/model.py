@@ -407,10 +407,14 @@ class B200LlamaModel(nn.Module):
             kbuf = torch.zeros(total_blocks, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
             vbuf = torch.zeros_like(kbuf)
             kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
-            for b in range(B):
-                s = starts[b] * BS
-                kf[s:s + lens[b]].copy_(kv_caches[b][li][0])
-                vf[s:s + lens[b]].copy_(kv_caches[b][li][1])
+            # every sequence's history into its blocks: one multi-tensor copy per layer
+            # instead of two copies per sequence
+            dst = [kf[starts[b] * BS:starts[b] * BS + lens[b]] for b in range(B) if lens[b]]
+            dst += [vf[starts[b] * BS:starts[b] * BS + lens[b]] for b in range(B) if lens[b]]
+            src = [kv_caches[b][li][0] for b in range(B) if lens[b]]
+            src += [kv_caches[b][li][1] for b in range(B) if lens[b]]
+            if dst:
+                torch._foreach_copy_(dst, [t.to(device=dev) for t in src])
             q, k, v = self._qkv(layer, h)
             ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
             attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,

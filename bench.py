@@ -556,16 +556,17 @@ def engine_mixed(args, dev, model):
     return res
 
 
-def engine_decode(args, dev, model, steps: int, warmup: int):
-    """The decode workload through B200Engine.step: the 64 sequences (contexts
+def engine_decode(args, dev, model, steps: int, warmup: int, ranks=None, rank: int = 0):
+    """The decode workload through B200Engine.step: this GPU's 64 sequences (contexts
     U{128..4096}, random token ids) are admitted and prefilled by the engine (untimed),
-    then `warmup` and `steps` engine steps decode all 64 at once, each step ending with
+    then `warmup` and `steps` engine steps decode all 64 at once, each step staging the
+    batch's positions and table rows in one pinned host-to-device copy and ending with
     its tokens on the host (the engine queues the next step on the device before it
-    reads them)."""
+    reads them).  With several ranks: barrier on both sides, the slowest rank's time."""
     import numpy as np
     from agentserve_b200 import B200Engine, Request
-    lens = context_lengths(args.batch, args.ctx_min, args.ctx_max, seed=0)
-    rng = np.random.default_rng(3)
+    lens = context_lengths(args.batch, args.ctx_min, args.ctx_max, seed=rank)
+    rng = np.random.default_rng(3 + rank)
     n_out = warmup + steps + 32  # nobody finishes inside the timed steps
     reqs = [Request(prompt="medium 100 decode", token_ids=rng.integers(3, 128000, L).tolist(),
                     max_tokens=n_out, request_id=f"d{i}") for i, L in enumerate(lens)]
@@ -578,6 +579,8 @@ def engine_decode(args, dev, model, steps: int, warmup: int):
         eng.step()
     for _ in range(warmup):
         eng.step()
+    if ranks is not None:
+        ranks.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     out0 = sum(r.num_output_tokens for r in reqs)
@@ -586,8 +589,14 @@ def engine_decode(args, dev, model, steps: int, warmup: int):
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     made = sum(r.num_output_tokens for r in reqs) - out0
-    res = {"value": made / wall, "unit": "tok/s", "steps": steps, "sequences": len(reqs),
-           "ms_per_step": wall / steps * 1e3,
+    world = 1
+    if ranks is not None:
+        ranks.barrier()
+        wall = ranks.max(wall)
+        world = ranks.world
+    res = {"value": world * made / wall, "unit": "tok/s", "steps": steps,
+           "sequences": world * len(reqs), "ms_per_step": wall / steps * 1e3,
+           "h2d_bytes_per_step": 3 * 4 * len(reqs), "d2h_bytes_per_step": 8 * len(reqs),
            "queued_decode_steps": dict(eng.spec_stats),
            "api": "B200Engine.step (scheduler, bookkeeping, one pinned copy of positions "
                   "and table rows in, the tokens out, every step)"}
@@ -976,7 +985,7 @@ def run_b200(args):
     # ---------------- end to end through forward_decode_paged with host lists
     e2e_n = max(1, args.e2e_steps - 2)
     e2e_s = ranks.max(run.e2e_steps(ranks, e2e_n))
-    e2e_value = (world // tp) * B * e2e_n / e2e_s
+    e2e_call = (world // tp) * B * e2e_n / e2e_s
 
     # ---------------- paged decode attention kernel alone (roofline)
     att = run.attention_alone()
@@ -987,6 +996,31 @@ def run_b200(args):
     del run
     gc.collect()
     torch.cuda.empty_cache()
+
+    # ---------------- end to end through B200Engine.step (every rank its own engine)
+    e2e_engine = None
+    if tp == 1 and args.model == "1b" and not args.no_engine:
+        e2e_engine = _optional("e2e engine", lambda: engine_decode(
+            args, dev, model, max(args.steps, 20), max(args.warmup, 3), ranks, rank))
+    if e2e_engine is not None and "error" not in e2e_engine:
+        e2e = {"value": e2e_engine["value"], "unit": "tok/s",
+               "api": "B200Engine.step on the same 64 sequences per GPU (scheduler, "
+                      "bookkeeping, greedy, one pinned copy of positions and table rows in "
+                      "and the tokens out every step; the next step queued on the device "
+                      "before the host reads this one's tokens)",
+               "h2d_bytes_per_step": e2e_engine["h2d_bytes_per_step"] * (world // tp),
+               "d2h_bytes_per_step": e2e_engine["d2h_bytes_per_step"] * (world // tp),
+               "ms_per_step": e2e_engine["ms_per_step"],
+               "queued_decode_steps": e2e_engine["queued_decode_steps"]}
+    else:
+        e2e = None
+    e2e_model_call = {"value": e2e_call, "unit": "tok/s",
+                      "api": "B200LlamaModel.forward_decode_paged(host lists) + greedy + .cpu()",
+                      # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
+                      # the greedy int64 tokens out
+                      "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8}
+    if e2e is None:
+        e2e = e2e_model_call
 
     # ---------------- the same 64 sequences split over the N GPUs (strong scaling)
     def strong_scaling():
@@ -1034,9 +1068,7 @@ def run_b200(args):
                         "U{17..1024} (seed 0), 512-block pool, 32/8 heads, head_dim 64, "
                         "fp32; the GPU also at batch 64 / 256 and in bf16"})
         if not args.no_engine and args.model == "1b":
-            engines = {"decode_through_engine": _optional("engine", lambda: engine_decode(
-                           args, dev, model, max(args.steps, 20), max(args.warmup, 3))),
-                       "mixed_requests": _optional("engine", lambda: engine_mixed(args, dev, model)),
+            engines = {"mixed_requests": _optional("engine", lambda: engine_mixed(args, dev, model)),
                        "prefix_cache_sessions": _optional("engine", lambda: engine_prefix(
                            args, dev, model, args.engine_sessions, args.engine_turns))}
         bits |= ops.device_status(clear=True)
@@ -1062,11 +1094,8 @@ def run_b200(args):
                          "algorithmic_bytes_per_launch": att["algorithmic_bytes_per_launch"],
                          "launch_ms": att["launch_ms"], "traffic": traffic_launch,
                          "traffic_source": (traffic or {}).get("source")},
-            "e2e": {"value": e2e_value, "unit": "tok/s",
-                    "api": "B200LlamaModel.forward_decode_paged(host lists) + greedy + .cpu()",
-                    # one pinned int32 [3, B] copy in (tokens, lengths, table rows),
-                    # the greedy int64 tokens out
-                    "h2d_bytes_per_step": 3 * B * 4, "d2h_bytes_per_step": B * 8},
+            "e2e": e2e,
+            "e2e_model_call": e2e_model_call,
             # per step: pack + first RMSNorm + greedy argmax + per layer (RoPE/cache +
             # attention in one launch, or two, 2 x add+RMSNorm, SwiGLU); the projections
             # and lm_head are cuBLAS
