@@ -84,6 +84,7 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       int64_t y_stride, int M, int Mpad, int N, int k_steps, int k_splits,
                       int* status) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  pdl_trigger();  // the next kernel may start its prologue; it waits for this one
   const int n_tile = blockIdx.x;
   const int split = blockIdx.y;
   const int s0 = int(int64_t(split) * k_steps / k_splits);
@@ -127,9 +128,21 @@ linear_small_m_kernel(const __grid_constant__ CUtensorMap tmap_w,
       tma_prefetch_desc(&tmap_x);
       const uint64_t pol_w = l2_policy_evict_first();  // each weight is read once
       const uint64_t pol_x = l2_policy_evict_last();   // X is re-read by every CTA
-      for (int i = 0; i < nsteps; ++i) {
+      // The weights do not depend on the previous kernel: the first ring's worth of W
+      // boxes is requested before the programmatic-launch wait, X (its output) after.
+      const int early = nsteps < kStages ? nsteps : kStages;
+      for (int i = 0; i < early; ++i) {
+        mbar_arrive_expect_tx(&bars->full[i], uint32_t(sbytes));
+        tma_load_2d(smem + i * sbytes, &tmap_w, &bars->full[i], (s0 + i) * kTileK,
+                    n_tile * kTileN, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < early; ++i)
+        tma_load_2d(smem + i * sbytes + kWBytes, &tmap_x, &bars->full[i], (s0 + i) * kTileK, 0,
+                    pol_x);
+      for (int i = early; i < nsteps; ++i) {
         const int st = i % kStages;
-        if (i >= kStages && !mbar_wait(&bars->empty[st], ((i / kStages) + 1) & 1, status)) {
+        if (!mbar_wait(&bars->empty[st], ((i / kStages) + 1) & 1, status)) {
           *abort_flag = 1;
           break;
         }
@@ -300,13 +313,15 @@ int launch_linear(void* y, int64_t y_stride, const void* x, int64_t x_stride, co
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = k_splits;  // the K splits of one N tile
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = AS_PDL;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaLaunchKernelEx(&cfg, kern, mw, mx, static_cast<T*>(y), y_stride, M, Mpad, N, k_steps,
                      k_splits, device_status_ptr());
   return check_launch("as_linear_small_m");
