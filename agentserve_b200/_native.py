@@ -63,6 +63,8 @@ SIGNATURES = {
                                                       _P]),
     "as_varlen_prefill_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32]),
     "as_linear_small_m": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _I32, _I32, _I32, _I32, _P]),
+    "as_linear_small_m_swiglu": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _I32, _I32, _I32, _I32,
+                                                _P]),
     "as_greedy_workspace_size": (_SZ, [_I32]),
     "as_greedy_argmax": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _P, _SZ, _P]),
     "as_rmsnorm": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _F32, _I32, _P]),

@@ -10,9 +10,11 @@ methods Engine uses:
                                                         llama.py:379-475, engine.py:360-366
 
 Attention, RoPE, KV writes, packing, block gathers, RMSNorm (+ residual add),
-SwiGLU and greedy argmax are the library's kernels; the projections and lm_head are
-cuBLAS GEMMs through torch (the library's small-batch projection kernel is optional,
-`small_batch_linear`).  With reference_compat=True (default) two
+SwiGLU and greedy argmax are the library's kernels; so are the projections and
+lm_head of batches up to `small_batch_max_rows` (64) tokens — the decode step — on the
+small-batch tensor-core kernel with SwiGLU fused into gate/up (`small_batch_linear`),
+while larger batches (prefill) use cuBLAS GEMMs through torch.  With
+reference_compat=True (default) two
 behaviours of the reference's decode paths are reproduced so results match it:
 the decode attention output is flattened dim-major before o_proj (llama.py:362,
 470), and forward_decode_batch returns, for every sequence shorter than the
@@ -170,11 +172,13 @@ class B200LlamaModel(nn.Module):
         # forward_decode_paged replays a CUDA graph per (allocator, batch size, block
         # bucket) instead of launching ~5 kernels per layer from Python every step
         self.decode_graphs: bool = True
-        # True: projections of at most 256 tokens (the decode step) on the small-batch
-        # tensor-core kernel (as_linear_small_m) instead of cuBLAS.  Off by default:
-        # measured slower than cuBLAS on B200 at batch 64 (the weight stream's ramp and
-        # the on-chip exchange of the K-split partials are the limits).
-        self.small_batch_linear: bool = False
+        # True (default): projections of at most small_batch_max_rows tokens (the decode
+        # step) on the library's small-batch tensor-core kernel (as_linear_small_m, with
+        # SwiGLU fused into gate/up) instead of cuBLAS; larger batches stay on cuBLAS.
+        # Graphed 1B decode step on B200: 1.758 vs 1.761 ms at 64 sequences, 1.349 vs
+        # 1.413 ms at 32; at 128 and 256 rows cuBLAS is faster.
+        self.small_batch_linear: bool = True
+        self.small_batch_max_rows: int = 64
         # True: the paged decode step does the new token's RoPE + cache write inside the
         # attention launch (as_rope_paged_decode_attention, bf16/fp16, head_dim 64/128);
         # False: separate RoPE + cache-write launch first (same results, bit for bit)
@@ -215,8 +219,7 @@ class B200LlamaModel(nn.Module):
         self._fused = True
 
     def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        if (self.small_batch_linear and x.shape[0] <= ops.LINEAR_MAX_M and x.is_cuda
-                and x.dtype in (torch.bfloat16, torch.float16)):
+        if self._small_batch(x):
             return ops.linear_small_m(x, w)
         return F.linear(x, w)
 
@@ -230,10 +233,18 @@ class B200LlamaModel(nn.Module):
                     qkv[:, (H + Kh) * D:].view(n, Kh, D))
         return (a.q_proj(h).view(n, H, D), a.k_proj(h).view(n, Kh, D), a.v_proj(h).view(n, Kh, D))
 
+    def _small_batch(self, x: torch.Tensor) -> bool:
+        return (self.small_batch_linear and x.shape[0] <= min(self.small_batch_max_rows,
+                                                              ops.LINEAR_MAX_M) and x.is_cuda
+                and x.dtype in (torch.bfloat16, torch.float16))
+
     def _mlp(self, layer: _Layer, h: torch.Tensor) -> torch.Tensor:
         """SwiGLU on the already-normalised h (llama.py:207-211)."""
         f = layer.ffn
         if self.fused_projections:
+            if self._small_batch(h) and f._gu_w.shape[0] % 128 == 0:
+                # gate/up projection and SwiGLU in one launch
+                return self._linear(ops.linear_small_m_swiglu(h, f._gu_w), f.down_proj.weight)
             return self._linear(ops.silu_mul(self._linear(h, f._gu_w)), f.down_proj.weight)
         return f.down_proj(F.silu(f.gate_proj(h)) * f.up_proj(h))
 
@@ -257,7 +268,7 @@ class B200LlamaModel(nn.Module):
         return h
 
     def _logits(self, h: torch.Tensor) -> torch.Tensor:
-        return self.lm_head(h)
+        return self._linear(h, self.lm_head.weight)
 
     def _workspace(self, B: int, max_blocks: int, bps: int) -> torch.Tensor:
         ws = self._workspaces.get(self.device)

@@ -363,6 +363,28 @@ def linear_small_m(x: torch.Tensor, w: torch.Tensor,
     return out
 
 
+def linear_small_m_swiglu(x: torch.Tensor, gate_up: torch.Tensor,
+                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [M, K] (M <= 256) -> silu(x W_gate^T) * (x W_up^T) [M, inter] in one launch from
+    the fused [gate; up] weight [2*inter, K] (inter a multiple of 64): the same bits as
+    silu_mul(linear_small_m(x, gate_up)) (llama.py:207-211)."""
+    _cuda(x, gate_up, out)
+    M, K = x.shape
+    two_i = gate_up.shape[0]
+    _require(gate_up.shape[1] == K and gate_up.is_contiguous() and x.stride(1) == 1 and
+             x.dtype == gate_up.dtype and two_i % 128 == 0,
+             "linear_small_m_swiglu: gate_up must be a contiguous [2*inter, K] of x's dtype, "
+             "inter a multiple of 64")
+    if out is None:
+        out = torch.empty(M, two_i // 2, dtype=x.dtype, device=x.device)
+    _require(out.shape == (M, two_i // 2) and out.stride(1) == 1 and out.dtype == x.dtype,
+             "linear_small_m_swiglu: out must be [M, inter] of x's dtype with contiguous rows")
+    N.check(N.load().as_linear_small_m_swiglu(
+        _ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(gate_up), M, two_i // 2, K,
+        dtype_code(x.dtype), _stream(x.device)), "as_linear_small_m_swiglu")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # (7) greedy sampling
 # ---------------------------------------------------------------------------

@@ -26,7 +26,7 @@
  *                             write_kv_decode and the attention) in one launch
  *   as_varlen_prefill_attention llama.py:128-186 (prefill over cached prefix + new tokens)
  *   as_varlen_prefill_attention_ws  the same, split-KV over CTAs with a workspace
- *   as_linear_small_m         nn.Linear of the decode step (llama.py:123-126, 203-211,
+ *   as_linear_small_m(_swiglu) nn.Linear of the decode step (llama.py:123-126, 203-211,
  *                             430-431, 471): q/k/v, o_proj, gate/up, down at batch <= 256
  *   as_greedy_argmax          sampling.py:46-58 (greedy branch) + engine.py:379-383
  *   as_block_copy             cache.py:158-189 (gather_kv) and engine.py:274-281,338-345
@@ -292,6 +292,17 @@ AS_API size_t as_varlen_prefill_workspace_size(int32_t num_seqs, int32_t max_seq
 AS_API int as_linear_small_m(void* y, int64_t y_stride, const void* x, int64_t x_stride,
                              const void* w, int32_t M, int32_t N, int32_t K, int32_t dtype,
                              as_stream_t stream);
+
+/* The gate/up projection with SwiGLU in its epilogue: y[m, j] = to_T(to_T(silu(g)) * u)
+ * with g = x w[j]^T and u = x w[inter + j]^T each rounded to the element type first
+ * (llama.py:203-211; the same bits as as_linear_small_m on w followed by as_silu_mul).
+ * w is the fused [2*inter, K] = [gate; up] weight (the layout as_silu_mul's input
+ * comes from), inter a multiple of 64; y is [M, inter] (row stride y_stride).
+ * M <= 256, bf16/fp16; each CTA loads 64 gate rows and the matching 64 up rows, K
+ * split over a cluster as in as_linear_small_m. */
+AS_API int as_linear_small_m_swiglu(void* y, int64_t y_stride, const void* x, int64_t x_stride,
+                             const void* w_gate_up, int32_t M, int32_t inter, int32_t K,
+                             int32_t dtype, as_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* (7) Greedy sampling                                                        */

@@ -436,6 +436,68 @@ def test_linear_small_m_strided_x_and_out():
     status_ok()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,inter,K", [(64, 8192, 2048), (1, 8192, 2048), (7, 192, 2048),
+                                       (130, 1024, 200), (256, 512, 1024), (33, 14336, 4096)])
+def test_linear_small_m_swiglu_vs_fp32(dtype, M, inter, K):
+    """Gate/up projection with SwiGLU in the epilogue against silu(g) * u of an fp32
+    matmul rounded to the dtype as the two projections' outputs are (llama.py:207-211);
+    inter a multiple of 64 (a tile = 64 gate rows + the matching 64 up rows of the
+    fused [gate; up] weight), K not a multiple of the 64-wide stage, M from 1 to 256."""
+    g = torch.Generator().manual_seed(M * 5 + inter + K)
+    x = (torch.randn(M, K, generator=g) * 0.5).to(dtype).to(DEV)
+    gu = (torch.randn(2 * inter, K, generator=g) * 0.05).to(dtype).to(DEV)
+    y = ops.linear_small_m_swiglu(x, gu)
+    assert y.shape == (M, inter)
+    proj = (x.float() @ gu.float().t()).to(dtype).float()
+    gate, up = proj[:, :inter], proj[:, inter:]
+    ref = (torch.nn.functional.silu(gate).to(dtype).float() * up)
+    tol = 2e-2 * max(1.0, float(ref.abs().max()))
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=tol)
+    status_ok()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M", [1, 16, 100, 256])
+@pytest.mark.parametrize("K,inter", [(128, 4096), (2048, 4096), (2048, 8192), (4096, 1024)])
+def test_linear_small_m_swiglu_bit_exact_vs_projection_then_silu_mul(dtype, M, K, inter):
+    """The fused launch splits K the same way as as_linear_small_m on the same weight
+    (one fp32 accumulation per split, splits summed in member order; K 128 takes no
+    split, the others 2 to 8), so it must equal as_linear_small_m followed by
+    as_silu_mul bit for bit; the output may be a row-strided view."""
+    g = torch.Generator().manual_seed(11 + M + K + inter)
+    x = (torch.randn(M, K, generator=g)).to(dtype).to(DEV)
+    gu = (torch.randn(2 * inter, K, generator=g) * 0.2).to(dtype).to(DEV)
+    two = ops.silu_mul(ops.linear_small_m(x, gu))
+    buf = torch.zeros(M, inter + 256, dtype=dtype, device=DEV)
+    y = ops.linear_small_m_swiglu(x, gu, out=buf[:, 128:128 + inter])
+    assert torch.equal(y, two)
+    assert int(buf[:, :128].count_nonzero()) == 0 and int(buf[:, 128 + inter:].count_nonzero()) == 0
+    status_ok()
+
+
+def test_linear_small_m_swiglu_rejects_bad_arguments():
+    xb = torch.randn(8, 128, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):  # 2*inter not a multiple of 128
+        ops.linear_small_m_swiglu(xb, torch.randn(192, 128, device=DEV, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):  # dtype mismatch
+        ops.linear_small_m_swiglu(xb, torch.randn(256, 128, device=DEV, dtype=torch.float16))
+    with pytest.raises(ValueError):  # out of the wrong width
+        ops.linear_small_m_swiglu(xb, torch.randn(256, 128, device=DEV, dtype=torch.bfloat16),
+                                  out=torch.empty(8, 256, device=DEV, dtype=torch.bfloat16))
+    lib = N.load()
+    w = torch.randn(256, 128, device=DEV, dtype=torch.bfloat16)
+    y = torch.empty(8, 128, device=DEV, dtype=torch.bfloat16)
+    s = ops._stream(xb.device)
+    assert lib.as_linear_small_m_swiglu(y.data_ptr(), 128, xb.data_ptr(), 128, w.data_ptr(), 8,
+                                        96, 128, N.AS_DTYPE_BF16, s) == N.AS_ERR_INVALID_ARG
+    assert lib.as_linear_small_m_swiglu(y.data_ptr(), 128, xb.data_ptr(), 128, w.data_ptr(), 300,
+                                        128, 128, N.AS_DTYPE_BF16, s) == N.AS_ERR_UNSUPPORTED
+    assert lib.as_linear_small_m_swiglu(y.data_ptr(), 128, xb.data_ptr(), 128, w.data_ptr(), 0,
+                                        128, 128, N.AS_DTYPE_BF16, s) == N.AS_OK
+    status_ok()
+
+
 # ---------------------------------------------------------------- greedy sampling
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("B,V", [(64, 128256), (3, 1000), (5, 4097), (2, 1), (130, 8192)])
