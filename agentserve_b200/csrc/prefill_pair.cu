@@ -7,10 +7,10 @@
 // the paged pool.
 //
 // CTA = (pair of query tiles, KV head g, sequence).  Query tile i (i = 0, 1) holds
-// 128 rows = tq tokens x the `group` query heads of KV head g.  Per KV tile of 128
-// keys (8 paged blocks) the K and V boxes land in shared memory once and feed both
-// query tiles, halving TMA work and shared-memory traffic per query row compared
-// with one tile per CTA.  Warp roles (320 threads, one CTA per SM):
+// 128 rows = tq tokens x the `group` query heads of KV head g.  Per KV tile (128 keys
+// = 8 paged blocks at head_dim 64, 64 keys = 4 blocks at 128) the K and V boxes land
+// in shared memory once and feed both query tiles, halving TMA work and shared-memory
+// traffic per query row compared with one tile per CTA.  Warp roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: both Q tiles once, then K/V tiles into a 4-stage ring;
 //   warp 1      MMA issuer (one thread), polling: S_i = Q_i K^T (both operands from
 //               shared memory, 128B swizzle) as soon as tile j's K/V is in and
@@ -23,8 +23,8 @@
 //               pairs and stored to TMEM with tcgen05.st.  The two warps that share an
 //               SM sub-partition take turns on its exponent unit (ping-pong), so one
 //               warp's TMEM loads, stores and waits overlap the other's exponentials.
-// TMEM (512 columns): tile i owns [256 i, 256 i + 256): S 128 columns, P 64 columns
-// (128 keys as 16-bit pairs), O D columns (at D=128 P overlays S; see PairCfg).
+// TMEM (512 columns): tile i owns [256 i, 256 i + 256): S one column per key of the
+// KV tile, P half as many (16-bit pairs), O D columns (see PairCfg).
 // Every wait is bounded; a wait that
 // runs out sets status bit 4, the CTA stops issuing, drains its MMAs, frees TMEM
 // and writes nothing.
@@ -90,6 +90,7 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 #ifndef AS_PREFILL_POLY_EVERY
 #define AS_PREFILL_POLY_EVERY 0  // 0: every exponential on the exponent unit
 #endif
+#if AS_PREFILL_POLY_EVERY > 0
 __device__ __forceinline__ uint64_t f2_add_rm(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -118,6 +119,7 @@ __device__ __forceinline__ uint64_t exp2_poly_f2(uint64_t x2) {
   const float eb = __uint_as_float(__float_as_uint(pb) + (__float_as_uint(rb) << 23));
   return f2_pack(ea, eb);
 }
+#endif
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
@@ -125,28 +127,46 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+// Keys per KV tile at head_dim 128: 128 (default) or 64.  With 128, S (128 columns)
+// and O (128) fill a query tile's 256 TMEM columns, so P must alias S and S(j+1) can
+// only be issued after PV(j) has read P(j); with 64, S, P and O sit side by side and
+// S(j+1) overlaps the softmax of tile j, but the S MMAs run at N=64 and every
+// per-tile cost is paid twice as often: measured on B200 (8 requests of 14,336 cached
+// + 600 new tokens) 683 TFLOP/s against 752 with 128-key tiles.
+#ifndef AS_PREFILL_BN128
+#define AS_PREFILL_BN128 128
+#endif
+#ifndef AS_PREFILL_STAGES128
+#define AS_PREFILL_STAGES128 4  // ring stages at head_dim 128 with 64-key tiles (<= 5 fit)
+#endif
+
 template <int HD>
 struct PairCfg {
   static constexpr int D = HD;
   static constexpr int kBM = 128;
-  static constexpr int kBN = 128;
+  static constexpr int kBN = D == 128 ? AS_PREFILL_BN128 : 128;  // keys per KV tile
+  static constexpr int kBlocks = kBN / kBS;       // paged blocks per KV tile
   static constexpr int kSub = D / 64;             // 64-element (128 B) swizzle sub-tiles
-  static constexpr int kSubBytes = 128 * 128;     // 128 rows x 128 B
-  static constexpr int kQBytes = kSub * kSubBytes;   // one query tile
-  static constexpr int kKVBytes = kSub * kSubBytes;  // K (or V) of one KV tile
-  static constexpr int kStages = D == 64 ? AS_PREFILL_PAIR_STAGES : 2;
+  static constexpr int kSubBytes = 128 * 128;     // Q sub-tile: 128 rows x 128 B
+  static constexpr int kKVSubBytes = kBN * 128;   // K/V sub-tile: kBN keys x 128 B
+  static constexpr int kQBytes = kSub * kSubBytes;     // one query tile
+  static constexpr int kKVBytes = kSub * kKVSubBytes;  // K (or V) of one KV tile
+  static constexpr int kStages =
+      D == 64 ? AS_PREFILL_PAIR_STAGES : (kBN == 64 ? AS_PREFILL_STAGES128 : 2);
   static constexpr int kOffQ = 0;                    // Q tile i at kOffQ + i * kQBytes
   static constexpr int kOffKV = 2 * kQBytes;         // stage s: K at +2s*kKVBytes, V after it
   static constexpr int kOffBar = kOffKV + kStages * 2 * kKVBytes;
   static constexpr int kSmemBytes = kOffBar + 512;
   static constexpr int kThreads = 320;
   static constexpr int kTmemCols = 512;
-  // TMEM columns of query tile i, from 256 i: S [0, 128); at D=64 P [128, 192) and
-  // O [192, 256); at D=128 O [128, 256) and P aliased onto S [0, 64) (S(j+1) is then
-  // issued only after PV(j), which reads P, in the MMA thread's in-order pipeline).
-  static constexpr bool kAliasP = D == 128;
-  static constexpr int kColP = kAliasP ? 0 : 128;
-  static constexpr int kColO = kAliasP ? 128 : 192;
+  // TMEM columns of query tile i, from 256 i: S [0, kBN), P [kBN, kBN + kBN / 2) (16-bit
+  // pairs), O [256 - D, 256); at D=128 with 128-key tiles P is aliased onto S [0, 64)
+  // (S(j+1) is then issued only after PV(j), which reads P, in the MMA thread's
+  // in-order pipeline).
+  static constexpr bool kAliasP = kBN + kBN / 2 > 256 - D;
+  static constexpr int kColP = kAliasP ? 0 : kBN;
+  static constexpr int kColO = 256 - D;
+  static_assert(kBN == 64 || kBN == 128, "KV tile");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -195,7 +215,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
   constexpr int D = Cfg::D;
   constexpr int NS = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = tc::idesc_f16(kBF16, 128, 128, false, false);
+  constexpr uint32_t kIdescS = tc::idesc_f16(kBF16, 128, Cfg::kBN, false, false);
   constexpr uint32_t kIdescO = tc::idesc_f16(kBF16, 128, D, false, true);
 
   const int r = blockIdx.z;
@@ -293,8 +313,9 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
           tma_load_3d(smem + Cfg::kOffQ + qi * Cfg::kQBytes + sb * Cfg::kSubBytes, &tmap_q,
                       &bars->q_full, sb * 64, g * group, q_begin + t0 + qi * tq, pol_q);
     }
+    constexpr int NB = Cfg::kBlocks;  // paged blocks per KV tile
     auto load_id = [&](int jt) -> int {
-      const int blk = 8 * jt + (lane & 7);
+      const int blk = NB * jt + (lane & (NB - 1));
       int id = fill_ok;  // keys past the sequence: finite filler data, masked to p = 0
       if (blk < nblk_seq) {
         id = __ldg(bt + int64_t(r) * bt_stride + blk);
@@ -318,7 +339,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const int id = id_next;
       if (j + 1 < n_load) id_next = load_id(j0 + j + 1);
       const int id0 = __shfl_sync(0xffffffffu, id, 0);
-      const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & 7));
+      const bool run8 = run8_ok && __all_sync(0xffffffffu, id == id0 + (lane & (NB - 1)));
       if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * Cfg::kKVBytes);
       __syncwarp();
       uint8_t* kst = smem + Cfg::kOffKV + st * 2 * Cfg::kKVBytes;
@@ -326,18 +347,18 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         if (lane == 0) {
 #pragma unroll
           for (int sb = 0; sb < Cfg::kSub; ++sb) {
-            tma_load_4d(kst + sb * Cfg::kSubBytes, &tmap_k8, &bars->kv_full[st], sb * 64, g, 0,
+            tma_load_4d(kst + sb * Cfg::kKVSubBytes, &tmap_k8, &bars->kv_full[st], sb * 64, g, 0,
                         id0, pol_kv);
-            tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kSubBytes, &tmap_v8, &bars->kv_full[st],
-                        sb * 64, g, 0, id0, pol_kv);
+            tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kKVSubBytes, &tmap_v8,
+                        &bars->kv_full[st], sb * 64, g, 0, id0, pol_kv);
           }
         }
-      } else if (lane < 8) {
+      } else if (lane < NB) {
 #pragma unroll
         for (int sb = 0; sb < Cfg::kSub; ++sb) {
-          tma_load_4d(kst + sb * Cfg::kSubBytes + lane * 2048, &tmap_k, &bars->kv_full[st],
+          tma_load_4d(kst + sb * Cfg::kKVSubBytes + lane * 2048, &tmap_k, &bars->kv_full[st],
                       sb * 64, g, 0, id, pol_kv);
-          tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kSubBytes + lane * 2048, &tmap_v,
+          tma_load_4d(kst + Cfg::kKVBytes + sb * Cfg::kKVSubBytes + lane * 2048, &tmap_v,
                       &bars->kv_full[st], sb * 64, g, 0, id, pol_kv);
         }
       }
@@ -354,9 +375,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         const uint32_t k = sKV + st * 2 * Cfg::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Cfg::kSubBytes + (kk & 3) * 32;
-          tc::mma_f16(tmem + 256 * i, tc::sdesc_sw128(q + off, 16, 1024),
-                      tc::sdesc_sw128(k + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          const uint32_t oq = (kk >> 2) * Cfg::kSubBytes + (kk & 3) * 32;
+          const uint32_t ok_ = (kk >> 2) * Cfg::kKVSubBytes + (kk & 3) * 32;
+          tc::mma_f16(tmem + 256 * i, tc::sdesc_sw128(q + oq, 16, 1024),
+                      tc::sdesc_sw128(k + ok_, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int i, int st, bool acc) {
@@ -365,7 +387,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         const uint32_t tO = tmem + 256 * i + Cfg::kColO;
 #pragma unroll
         for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
-          tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kSubBytes, 1024),
+          tc::mma_f16_ts(tO, tP + kk * 8, tc::sdesc_sw128(v + kk * 2048, Cfg::kKVSubBytes, 1024),
                          kIdescO, (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->q_full, 0, status, wait_limit);
@@ -443,36 +465,32 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         break;
       }
       tc::fence_after_sync();
-      float x[128];
+      constexpr int BN = Cfg::kBN;
+      float x[BN];
       {
-        uint32_t v0[32], v1[32], v2[32], v3[32];
-        tc::ld_32x32b_x32(tS + 0, v0);
-        tc::ld_32x32b_x32(tS + 32, v1);
-        tc::ld_32x32b_x32(tS + 64, v2);
-        tc::ld_32x32b_x32(tS + 96, v3);
+        uint32_t v[BN / 32][32];
+#pragma unroll
+        for (int u = 0; u < BN / 32; ++u) tc::ld_32x32b_x32(tS + 32 * u, v[u]);
         tc::wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          x[c] = __uint_as_float(v0[c]);
-          x[32 + c] = __uint_as_float(v1[c]);
-          x[64 + c] = __uint_as_float(v2[c]);
-          x[96 + c] = __uint_as_float(v3[c]);
-        }
+        for (int u = 0; u < BN / 32; ++u)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) x[32 * u + c] = __uint_as_float(v[u][c]);
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_free[i]);  // S(j+1) may overwrite S now
 
       const int lim = qpos - (j0 + j) * Cfg::kBN;  // keys c <= lim are visible
-      if (lim < Cfg::kBN - 1) {
+      if (lim < BN - 1) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
+        for (int c = 0; c < BN; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
       }
       float mp[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mp[c] = fmaxf(x[c], x[8 + c]);
 #pragma unroll
-      for (int c = 16; c < 128; c += 16) {
+      for (int c = 16; c < BN; c += 16) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) mp[e] = max3f(mp[e], x[c + e], x[c + 8 + e]);
       }
@@ -503,9 +521,11 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(neg_m, neg_m);
       uint64_t sp2[4] = {0, 0, 0, 0};  // 8 independent fp32 partial sums, as pairs
-      uint32_t pk[64];
+      uint32_t pk[BN / 2];
+      // the exponent-unit turn passes on after AS_PREFILL_HANDOFF of every 64 pairs
+      constexpr int kHand = AS_PREFILL_HANDOFF * BN / 128;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < BN / 2; ++c) {
         const uint64_t xs = f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2);
         float a, b;
         f2_unpack(xs, a, b);
@@ -520,7 +540,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         float p0, p1;
         f2_unpack(p2, p0, p1);
         pk[c] = pack2<T>(p0, p1);
-        if (AS_PREFILL_PINGPONG && AS_PREFILL_HANDOFF < 64 && c == AS_PREFILL_HANDOFF - 1) {
+        if (AS_PREFILL_PINGPONG && kHand < BN / 2 && c == kHand - 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
         }
@@ -532,7 +552,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         f2_unpack(s01, a, b);
         sum = a + b;
       }
-      if (AS_PREFILL_PINGPONG && AS_PREFILL_HANDOFF >= 64) {
+      if (AS_PREFILL_PINGPONG && kHand >= BN / 2) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->turn[1 - i][quad]);
       }
@@ -543,8 +563,9 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
         }
         tc::fence_after_sync();
       }
-      tc::st_32x32b_x32(tP, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-      tc::st_32x32b_x32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+#pragma unroll
+      for (int u = 0; u < BN / 64; ++u)
+        tc::st_32x32b_x32(tP + 32 * u, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32 * u]));
       l = l * alpha + sum;
       if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
@@ -712,7 +733,9 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
     const uint64_t strides[3] = {uint64_t(D) * es, uint64_t(Kh) * D * es,
                                  uint64_t(kBS) * Kh * D * es};
     const uint32_t box[4] = {64, 1, uint32_t(kBS), 1};
-    const uint32_t box8[4] = {64, 1, uint32_t(kBS), num_blocks >= 8 ? 8u : 1u};
+    // a whole KV tile of consecutive blocks in one box (the run fast path)
+    const uint32_t box8[4] = {64, 1, uint32_t(kBS),
+                              num_blocks >= Cfg::kBlocks ? uint32_t(Cfg::kBlocks) : 1u};
     int rc = encode_tensor_map(&mk, tmap_dtype<T>(), 4, const_cast<void*>(k_cache), dims, strides,
                                box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc)
@@ -740,7 +763,7 @@ int launch_pair(void* out, const void* q, int64_t q_stride, const void* k_cache,
   dim3 grid(npairs * n_split, Kh, R);
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
       mq, mk, mv, mk8, mv8, static_cast<T*>(out), bt, bt_stride, cu, lk, H, group, num_blocks,
-      max_blocks, scale * kLog2e, num_blocks >= 8 ? 1 : 0, n_split, part_o, part_ml,
+      max_blocks, scale * kLog2e, num_blocks >= Cfg::kBlocks ? 1 : 0, n_split, part_o, part_ml,
       device_status_ptr(), wait_limit_ns(), take_starve_flag(AS_KERNEL_PREFILL_ATTENTION) ? 1 : 0);
   int rc = check_launch("as_varlen_prefill_attention (tcgen05, query-tile pairs)");
   if (rc || n_split == 1) return rc;
