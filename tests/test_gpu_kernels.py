@@ -205,7 +205,8 @@ def test_decode_lowp_fast_path(dtype, D, bps):
                                           (8, 1, 128, torch.bfloat16), (4, 2, 16, torch.bfloat16),
                                           (4, 2, 16, torch.float32), (32, 8, 64, torch.float32),
                                           (32, 8, 128, torch.float32), (24, 8, 128, torch.float16),
-                                          (64, 4, 64, torch.bfloat16)])
+                                          (64, 4, 64, torch.bfloat16), (15, 3, 64, torch.bfloat16),
+                                          (16, 4, 128, torch.float16), (16, 2, 64, torch.bfloat16)])
 def test_decode_geometries(H, Kh, D, dtype):
     lens = [1, 16, 17, 300, 1025]
     tables, kp, vp, q = decode_case(lens, H, Kh, D, dtype, seed=H * Kh + D)
