@@ -922,7 +922,9 @@ def config5(args, dev, ranks: Ranks, rank: int, world: int) -> dict:
     run = DecodeRun(model, context_lengths(32, 1024, 32768, seed=500 + rank), warm + steps + 4,
                     0, seed=500 + rank)
     ms = ranks.max(run.timed_steps(ranks, steps, warm))
+    note_status("config5 replica steps")
     att = run.attention_alone(reps_per_layer=1)
+    note_status("config5 replica attention")
     res["replicas"] = {"sequences_per_gpu": 32, "n_gpus": world,
                        "value": world * 32 * steps / (ms / 1e3), "unit": "tok/s",
                        "ms_per_step": ms / steps,
@@ -938,6 +940,7 @@ def config5(args, dev, ranks: Ranks, rank: int, world: int) -> dict:
         run = DecodeRun(model, context_lengths(B, 1024, 32768, seed=600), warm + steps + 4, 0,
                         seed=600 + rank, token_seed=600)
         ms = ranks.max(run.timed_steps(ranks, steps, warm))
+        note_status("config5 tensor-parallel steps")
         att = run.attention_alone(reps_per_layer=1)
         ar = allreduce_ms(ranks, B, cfg.hidden_dim, dev)
         step_ms = ms / steps
@@ -988,6 +991,21 @@ def _optional(name: str, fn):
         return {"error": f"{type(e).__name__}: {e}"}
 
 
+_STATUS = {"bits": 0}
+
+
+def note_status(tag: str) -> int:
+    """Read and clear this rank's device status word (bit 4: a bounded wait ran out);
+    report a non-zero word on stderr with the section it follows; accumulate it."""
+    from agentserve_b200 import ops
+    bits = ops.device_status(clear=True)
+    if bits:
+        print(f"rank {os.environ.get('RANK', '0')}: device status bits {bits} after {tag}",
+              file=sys.stderr, flush=True)
+    _STATUS["bits"] |= bits
+    return bits
+
+
 def launches_per_step(model, cfg, batch: int) -> int:
     """The library's kernel launches in one graphed decode step: pack + first RMSNorm +
     greedy argmax (+ lm_head on the small-batch kernel), and per layer the RoPE/cache +
@@ -1036,9 +1054,10 @@ def run_b200(args):
     e2e_call = (world // tp) * B * e2e_n / e2e_s
 
     # ---------------- paged decode attention kernel alone (roofline)
+    note_status("the timed decode steps and the end-to-end model calls")
     att = run.attention_alone()
     peak, peak_kind = measured_peaks()
-    bits = ops.device_status(clear=True)
+    note_status("the attention-alone launches")
     model.release_decode_graphs()
     run.free()
     del run
@@ -1055,6 +1074,7 @@ def run_b200(args):
             return engine_decode(args, dev, model, max(args.steps, 20), max(args.warmup, 3),
                                  ranks, rank)
         e2e_engine = _optional("e2e engine", e2e_engine_run)
+        note_status("the engine end-to-end steps")
     if e2e_engine is not None and "error" not in e2e_engine:
         e2e = {"value": e2e_engine["value"], "unit": "tok/s",
                "api": "B200Engine.step on the same 64 sequences per GPU (scheduler, "
@@ -1099,12 +1119,13 @@ def run_b200(args):
     strong = None
     if world > 1 and tp == 1 and not args.no_strong:
         strong = _optional("strong", strong_scaling)
+        note_status("the strong-scaling steps")
 
     # ---------------- 8B geometry: replicas, and KV-head TP over the N GPUs
     c5 = None
     if args.model == "1b" and tp == 1 and not args.no_config5:
         c5 = _optional("config5", lambda: config5(args, dev, ranks, rank, world))
-        bits |= ops.device_status(clear=True)
+        note_status("config5")
 
     pf = pf128 = c1 = engines = None
     if rank == 0 and world == 1 and tp == 1:
@@ -1125,8 +1146,12 @@ def run_b200(args):
             engines = {"mixed_requests": _optional("engine", lambda: engine_mixed(args, dev, model)),
                        "prefix_cache_sessions": _optional("engine", lambda: engine_prefix(
                            args, dev, model, args.engine_sessions, args.engine_turns))}
-        bits |= ops.device_status(clear=True)
+        note_status("prefill, config1 and the engine workloads")
 
+    status_per_rank = ranks.gather(_STATUS["bits"])
+    status_all = 0
+    for b_ in status_per_rank:
+        status_all |= b_
     ranks.barrier()
     if rank == 0:
         traffic = load_traffic() if args.model == "1b" else None
@@ -1168,7 +1193,8 @@ def run_b200(args):
                                  "frac": pf128["8x"]["tflops"] / bf16_peak}},
             "config1": c1,
             "engine": engines,
-            "clocks": clk, "device_status": bits,
+            "clocks": clk, "device_status": status_all,
+            "device_status_per_rank": status_per_rank,
         }
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_baseline(args, steps=args.cpu_sample_steps, warmup=1,
