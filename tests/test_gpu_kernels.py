@@ -404,13 +404,15 @@ def test_prefill_split_kv_auto_one_request_and_workspace_rules():
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("M,N,K", [(64, 3072, 2048), (1, 2048, 2048), (7, 16384, 2048),
                                    (64, 2048, 8192), (100, 130, 72), (128, 4096, 4096),
-                                   (200, 6144, 4096), (256, 512, 1024), (33, 1002, 4096)])
+                                   (200, 6144, 4096), (256, 512, 1024), (33, 1002, 4096),
+                                   (120, 1002, 4096), (128, 1002, 4096)])
 def test_linear_small_m_vs_fp32(dtype, M, N, K):
     """as_linear_small_m against an fp32 matmul of the same (rounded) inputs: N not a
     multiple of the 128-row tile (1002: the last split member's rows end mid-vector, and
     odd output rows take the element-wise store), K not a multiple of the 64-wide stage,
-    M from 1 to 256, clusters of 1 to 8 K splits; repeat calls bit-identical (splits are
-    summed in member order)."""
+    M from 1 to 256, clusters of 1 to 8 K splits, the split partials exchanged by push
+    (up to 120 rows here) and by pull (128 rows and more); repeat calls bit-identical
+    (splits are summed in member order)."""
     g = torch.Generator().manual_seed(M * 7 + N + K)
     x = (torch.randn(M, K, generator=g) * 0.5).to(dtype).to(DEV)
     w = (torch.randn(N, K, generator=g) * 0.05).to(dtype).to(DEV)
@@ -439,7 +441,8 @@ def test_linear_small_m_strided_x_and_out():
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("M,inter,K", [(64, 8192, 2048), (1, 8192, 2048), (7, 192, 2048),
-                                       (130, 1024, 200), (256, 512, 1024), (33, 14336, 4096)])
+                                       (130, 1024, 200), (256, 512, 1024), (33, 14336, 4096),
+                                       (120, 1024, 2048), (128, 1024, 2048)])
 def test_linear_small_m_swiglu_vs_fp32(dtype, M, inter, K):
     """Gate/up projection with SwiGLU in the epilogue against silu(g) * u of an fp32
     matmul rounded to the dtype as the two projections' outputs are (llama.py:207-211);
