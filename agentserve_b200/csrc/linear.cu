@@ -1,6 +1,7 @@
 // (6) Decode-step projections for a small batch: Y[M, N] = X[M, K] W[N, K]^T
 // (nn.Linear without bias: q/k/v, o_proj, gate/up, down at agentserve/model/llama.py:
-// 123-126, 203-211, 430-471), bf16/fp16 in, fp32 accumulation, M <= 256.
+// 123-126, 203-211, 430-471), bf16/fp16 in, fp32 accumulation, M <= 256; and the
+// gate/up projection with SwiGLU applied in the epilogue (llama.py:207-211).
 //
 // At decode batch sizes the product is a stream over the weights (2 bytes per weight,
 // 2*M FLOPs per weight): it has to read W at HBM bandwidth, which needs every SM busy
@@ -8,18 +9,26 @@
 // (K split), and each CTA computes D[128 x Mpad] = W_tile X^T on the tensor cores
 // (tcgen05.mma kind::f16, M=128, N=Mpad, both operands K-major 128B-swizzled in shared
 // memory, accumulator in TMEM) over its K range (M <= 256):
-//   warp 0     TMA producer: W box 128 rows x 64 K and X box Mpad rows x 64 K per stage
-//              (X rows >= M read as zeros), 4-stage ring;
+//   warp 0     TMA producer: W box 128 rows x 64 K (with SwiGLU two 64-row boxes: the
+//              tile's gate rows and the matching up rows) and X box Mpad rows x 64 K per
+//              stage (X rows >= M read as zeros), 4-stage ring; launched
+//              programmatically, it requests the first ring's W boxes before waiting
+//              for the kernel ahead (which produces X);
 //   warp 1     MMA issuer (one thread), commits each stage back to the producer;
 //   warps 2-5  epilogue, one TMEM lane (= weight row n) per thread: with one split it
-//              stores Y directly; with several it copies its fp32 partial tile into
-//              its own shared memory (over the drained stage ring).
-// The K splits of one N tile form a thread-block cluster (2, 4 or 8 CTAs): after a
-// cluster barrier, member r sums rows [r*128/splits, (r+1)*128/splits) of every
-// member's partial through distributed shared memory, in member order (deterministic),
-// and a second cluster barrier keeps the partials alive until all reads are done.  No
+//              stores Y (or silu(gate) * up) directly; with several it writes its fp32
+//              partial tile into its own shared memory (over the drained stage ring).
+// The K splits of one N tile form a thread-block cluster (2, 4 or 8 CTAs); member r
+// finishes rows [r*128/splits, (r+1)*128/splits) of the tile (with SwiGLU: that share
+// of the gate rows and the matching up rows), summing every member's partial of them
+// in member order (deterministic).  The partials are exchanged either by push — each
+// member bulk-copies slice r of its partial into member r's shared memory, completing
+// on r's mbarrier, after one cluster barrier that guarantees the receivers' rings are
+// drained — or, when the partial and the receive slots do not fit the ring together,
+// by pull: after a cluster barrier every member reads the slices over distributed
+// shared memory, and a second barrier keeps them alive until all reads are done.  No
 // global workspace, no atomics.  Every mbarrier wait is bounded (status bit 4); every
-// thread of every member reaches both cluster barriers on every path.
+// thread of every member reaches each cluster barrier on every path.
 #include <type_traits>
 
 #include "common.cuh"
