@@ -529,7 +529,6 @@ class B200LlamaModel(nn.Module):
         return g
 
     @torch.inference_mode()
-    @torch.inference_mode()
     def decode_paged_greedy(self, last_token_ids: List[int], seq_lens: List[int], allocator,
                             request_ids: List[str]) -> List[int]:
         """One greedy decode step of the batch (forward_decode_paged with position =
