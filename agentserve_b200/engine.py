@@ -149,6 +149,7 @@ class B200Engine:
         # its own prefix stored in the cache): never rewritten, not even when the
         # request is preempted and prefilled again
         self._frozen: Dict[str, int] = {}
+        self._hashes: Dict[str, tuple] = {}  # request id -> (prompt list, its block hashes)
         # queue the next decode step before reading this one's tokens (see _decode)
         self.speculative_decode: bool = True
         self._spec: Optional[_Speculation] = None
@@ -205,6 +206,16 @@ class B200Engine:
     def _release(self, req) -> None:
         self.allocator.free(req.request_id)
         self._frozen.pop(req.request_id, None)
+        self._hashes.pop(req.request_id, None)
+
+    def _prompt_hashes(self, req) -> List[int]:
+        """The prompt's chained block hashes, computed once per request (admission
+        peeks, then looks up, and the prefill stores a prefix of the same prompt)."""
+        h = self._hashes.get(req.request_id)
+        if h is None or h[0] is not req.token_ids:
+            h = self._hashes[req.request_id] = (req.token_ids,
+                                                self.prefix_cache.block_hashes(req.token_ids))
+        return h[1]
 
     # ------------------------------------------------------------------ admission
     def _classify(self, req) -> None:
@@ -226,7 +237,8 @@ class B200Engine:
         """engine.py:258-294, admitting a request only when its blocks fit."""
         while self._incoming:
             req = self._incoming[0]
-            matched, ids = self.prefix_cache.peek_longest_prefix(req.token_ids)
+            hashes = self._prompt_hashes(req)
+            matched, ids = self.prefix_cache.peek_longest_prefix(req.token_ids, hashes=hashes)
             if not self._fits(req, len(ids)):
                 keep = req.token_ids[:matched] if matched else None
                 while self.prefix_cache.size() > (1 if matched else 0) and \
@@ -243,7 +255,7 @@ class B200Engine:
                     return  # wait for running requests to finish
             self._incoming.popleft()
             self._classify(req)
-            matched, ids, _ = self.prefix_cache.find_longest_prefix(req.token_ids)
+            matched, ids, _ = self.prefix_cache.find_longest_prefix(req.token_ids, hashes=hashes)
             req.num_cached_tokens = matched
             if matched > 0:
                 self.metrics.prefix_cache_hits += 1
@@ -283,7 +295,8 @@ class B200Engine:
             n = len(req.token_ids) // bs * bs
             if n > 0:
                 ids = self.allocator.blocks_for(req.request_id)[:n // bs]
-                if self.prefix_cache.store(req.token_ids[:n], ids):
+                if self.prefix_cache.store(req.token_ids[:n], ids,
+                                           hashes=self._prompt_hashes(req)):
                     self._frozen[req.request_id] = max(self._frozen.get(req.request_id, 0), n)
 
     # ------------------------------------------------------------------ decode

@@ -18,6 +18,7 @@ reference (release_blocks).  No K/V byte moves.
 from __future__ import annotations
 
 import hashlib
+from collections import OrderedDict
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -74,29 +75,61 @@ class PrefixCache:
         self.stats = PrefixCacheStats()
         self._step = 0
         self._cache: Dict[int, PrefixEntry] = {}
-        self._token_to_hash: Dict[tuple, int] = {}
-        self._memo: Dict[bytes, List[int]] = {}
+        # recently hashed prompts (token list, chained hashes), keyed by their first
+        # block: a prompt that starts like one of them resumes its chain (multi-turn
+        # sessions and a shared system prefix rehash only their new blocks)
+        self._memo: "OrderedDict[tuple, Tuple[List[int], List[int]]]" = OrderedDict()
 
-    def _block_hashes(self, token_ids: Sequence[int]) -> List[int]:
-        """Chained hashes of every complete block (prefix_cache.py:94-104).  The last
-        few prompts' hashes are memoised (an admission peeks and then looks up)."""
-        n = len(token_ids) // self.block_size * self.block_size
-        key = np.asarray(token_ids[:n], dtype="<u4").tobytes()
-        hashes = self._memo.get(key)
-        if hashes is None:
-            hashes = _chain(key, self.block_size)
-            self._memo[key] = hashes
-            if len(self._memo) > 8:
-                self._memo.pop(next(iter(self._memo)))
+    def block_hashes(self, token_ids: Sequence[int]) -> List[int]:
+        """Chained hashes of every complete block (prefix_cache.py:94-104).  A caller
+        that looks a prompt up several times (peek, find, then store a prefix of it)
+        can compute them once and pass them as `hashes`; the last few prompts' hashes
+        are also memoised."""
+        bs = self.block_size
+        nb = len(token_ids) // bs
+        if nb == 0:
+            return []
+        toks = list(token_ids)
+        key = tuple(toks[:bs])
+        done, hashes = 0, []
+        hit = self._memo.get(key)
+        if hit is not None:
+            old, old_h = hit
+            # longest common prefix in whole blocks: 64 blocks at a time, then block
+            # by block inside the first chunk that differs
+            m = min(nb, len(old_h))
+            k = 0
+            while k + 64 <= m and toks[k * bs:(k + 64) * bs] == old[k * bs:(k + 64) * bs]:
+                k += 64
+            while k < m and toks[k * bs:(k + 1) * bs] == old[k * bs:(k + 1) * bs]:
+                k += 1
+            done, hashes = k, old_h[:k]
+        if done < nb:
+            prev = hashes[-1] if hashes else 0
+            tail = np.asarray(toks[done * bs:nb * bs], dtype="<u4").tobytes()
+            hashes = hashes + _chain(tail, bs, prev)
+        self._memo[key] = (toks, hashes)
+        self._memo.move_to_end(key)
+        if len(self._memo) > 64:
+            self._memo.popitem(last=False)
         return hashes
 
+    _block_hashes = block_hashes
+
+    def _hashes(self, token_ids: Sequence[int], hashes: Optional[Sequence[int]]) -> Sequence[int]:
+        if hashes is None:
+            return self.block_hashes(token_ids)
+        return hashes[:len(token_ids) // self.block_size]
+
     def store(self, token_ids: Sequence[int], block_ids: Sequence[int],
-              kv_tensors: Optional[list] = None) -> bool:
+              kv_tensors: Optional[list] = None,
+              hashes: Optional[Sequence[int]] = None) -> bool:
         """Cache a computed prefix of complete blocks whose K/V sit in block_ids
         (prefix_cache.py:110-149).  A prefix already cached only gets its counters
         bumped; otherwise the lowest-ranked entry is evicted when the cache is full.
-        Returns True when a new entry now holds these blocks."""
-        hashes = self._block_hashes(token_ids)
+        Returns True when a new entry now holds these blocks.  hashes: block_hashes()
+        of token_ids or of a longer prompt it begins (computed here if omitted)."""
+        hashes = self._hashes(token_ids, hashes)
         if not hashes:
             return False
         key = hashes[-1]
@@ -111,13 +144,13 @@ class PrefixCache:
         if self.allocator is not None:
             self.allocator.retain_blocks(ids)
         self._cache[key] = PrefixEntry(list(token_ids), ids, None, 1, self._step)
-        self._token_to_hash[tuple(token_ids)] = key
         return True
 
-    def peek_longest_prefix(self, token_ids: Sequence[int]) -> Tuple[int, List[int]]:
+    def peek_longest_prefix(self, token_ids: Sequence[int],
+                            hashes: Optional[Sequence[int]] = None) -> Tuple[int, List[int]]:
         """find_longest_prefix without counting it (no stats, no reuse bump): what a
         lookup would return now, for sizing an admission before making it."""
-        hashes = self._block_hashes(token_ids)
+        hashes = self._hashes(token_ids, hashes)
         for i in range(len(hashes) - 1, -1, -1):
             entry = self._cache.get(hashes[i])
             n = (i + 1) * self.block_size
@@ -125,11 +158,13 @@ class PrefixCache:
                 return n, list(entry.block_ids)
         return 0, []
 
-    def find_longest_prefix(self, token_ids: Sequence[int]) -> Tuple[int, List[int], None]:
+    def find_longest_prefix(self, token_ids: Sequence[int],
+                            hashes: Optional[Sequence[int]] = None
+                            ) -> Tuple[int, List[int], None]:
         """(matched tokens, block ids, None) for the longest cached prefix, or
         (0, [], None) (prefix_cache.py:151-183)."""
         self._step += 1
-        hashes = self._block_hashes(token_ids)
+        hashes = self._hashes(token_ids, hashes)
         for i in range(len(hashes) - 1, -1, -1):
             entry = self._cache.get(hashes[i])
             if entry is None:
@@ -152,7 +187,6 @@ class PrefixCache:
             ranked = [kv for kv in ranked if kv[1].token_ids != keep]
         for key, entry in ranked[:n]:
             del self._cache[key]
-            self._token_to_hash.pop(tuple(entry.token_ids), None)
             if self.allocator is not None:
                 self.allocator.release_blocks(entry.block_ids)
             self.stats.evictions += 1
@@ -169,4 +203,3 @@ class PrefixCache:
             for entry in self._cache.values():
                 self.allocator.release_blocks(entry.block_ids)
         self._cache.clear()
-        self._token_to_hash.clear()
