@@ -154,6 +154,44 @@ def test_prefix_cache_hash_and_matching():
     assert pc.peek_longest_prefix([1, 2, 3, 4, 5, 6, 7, 8])[0] == 8  # reused entry kept
 
 
+def _plain_chain(tokens, bs=16):
+    hs, prev = [], 0
+    for i in range(len(tokens) // bs):
+        prev = block_hash(tokens[i * bs:(i + 1) * bs], prev)
+        hs.append(prev)
+    return hs
+
+
+def test_block_hashes_resume_the_chain_of_a_recent_prompt_exactly():
+    """A prompt that begins like a recently hashed one reuses that chain up to the
+    longest common block-aligned prefix and hashes the rest: the result must equal the
+    chain computed from scratch (extensions, shared prefixes, a first difference inside
+    a 64-block chunk or at its edge, prompts shorter than a block, memo eviction)."""
+    rng = torch.Generator().manual_seed(0)
+    rand = lambda n: torch.randint(3, 50000, (n,), generator=rng).tolist()  # noqa: E731
+    pc = PrefixCache(block_size=16)
+    base = rand(16 * 200 + 5)
+    cases = [base, base + rand(40), base[:16 * 64] + rand(100), base[:16 * 64 + 7] + rand(50),
+             base[:16 * 63] + rand(16), base[:16 * 130 + 3], base[:10], base[:16],
+             rand(16 * 70) + base, base + rand(16 * 3)]
+    for t in cases:
+        assert pc.block_hashes(t) == _plain_chain(t), len(t)
+    for i in range(80):  # more first blocks than the memo holds
+        t = rand(16 * 3 + i)
+        assert pc.block_hashes(t) == _plain_chain(t)
+    assert pc.block_hashes(base + [1] * 16) == _plain_chain(base + [1] * 16)
+
+
+def test_precomputed_hashes_give_the_same_lookups_and_entries():
+    toks = list(range(1000, 1000 + 16 * 12 + 3))
+    a, b = PrefixCache(), PrefixCache()
+    hs = a.block_hashes(toks)
+    assert a.store(toks[:16 * 8], list(range(8)), hashes=hs) == b.store(toks[:16 * 8], list(range(8)))
+    assert a.peek_longest_prefix(toks, hashes=hs) == b.peek_longest_prefix(toks) == (128, list(range(8)))
+    assert a.find_longest_prefix(toks, hashes=hs) == b.find_longest_prefix(toks)
+    assert set(a._cache) == set(b._cache)
+
+
 def test_scheduler_modes_basic():
     s = Scheduler(max_batch_size=2, max_prefill_per_step=2)
     reqs = [Request(prompt="x", token_ids=[1], max_tokens=3, priority=p) for p in (2, 0, 1)]
