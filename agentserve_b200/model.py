@@ -166,6 +166,10 @@ class B200LlamaModel(nn.Module):
         self.decode_layout = N.AS_LAYOUT_DIM_MAJOR if reference_compat else N.AS_LAYOUT_HEAD_MAJOR
         self._fused = False
         self._workspaces = {}
+        # forward_decode_batch's block buffers, kept while the caller feeds back the
+        # caches it returned; free tokens each sequence gets when they are (re)packed
+        self._batch_pool: Optional[dict] = None
+        self.decode_batch_headroom: int = 64
         # decode attention split-K chunk in blocks: 0 = chosen by the library from the
         # batch's block count and the SM count (default); > 0 = fixed chunk
         self.decode_blocks_per_split: int = 0
@@ -384,63 +388,114 @@ class B200LlamaModel(nn.Module):
     @torch.inference_mode()
     def forward_decode_batch(self, last_token_ids: List[int], kv_caches: list,
                              position_offsets: List[int]):
-        """llama.py:265-376 with the per-request KV lists packed into one block buffer
-        per layer (each sequence gets its own 16-token blocks), the new token written
-        by the fused RoPE kernel and attention done by the paged decode kernel."""
+        """llama.py:265-376 with the per-request KV lists kept in one block buffer per
+        layer (each sequence its own run of 16-token blocks with some free blocks after
+        it), the new token written by the fused RoPE kernel and attention done by the
+        paged decode kernel.
+
+        The returned caches are views of those buffers.  When the next call passes them
+        back unchanged (same requests in the same order, each cache exactly the view
+        returned for it) and every sequence still has room, the histories are used in
+        place and only the new token is written; otherwise (a new batch, a request
+        whose run is full, caches from elsewhere) the histories are packed into new
+        buffers first, each sequence getting `decode_batch_headroom` free tokens."""
         self.fuse_projections_()
         B = len(last_token_ids)
         c = self.config
         if B == 0:
             return torch.zeros(0, c.vocab_size), []
         dev = self.device
+        L_layers = len(self.layers)
         lens = [int(kv_caches[b][0][0].shape[0]) for b in range(B)]
         max_len = max(lens)
-        nb = [(L + 1 + BS - 1) // BS for L in lens]
-        starts = [0]
-        for n in nb[:-1]:
-            starts.append(starts[-1] + n)
-        total_blocks = starts[-1] + nb[-1]
-        mb = max(nb)
-        bt_host = torch.zeros(B, mb, dtype=torch.int32)
-        for b in range(B):
-            bt_host[b, :nb[b]] = torch.arange(starts[b], starts[b] + nb[b], dtype=torch.int32)
-        bt = bt_host.to(dev)
+        pool = self._batch_pool
+        if not (pool is not None and pool["B"] == B and self._batch_pool_matches(pool, kv_caches, lens)):
+            pool = self._batch_pool = self._pack_batch(kv_caches, lens)
+        starts, kbufs, vbufs = pool["starts"], pool["k"], pool["v"]
         slots_host = [starts[b] * BS + lens[b] for b in range(B)]
         slots = torch.tensor(slots_host, dtype=torch.int64, device=dev)
         pos = torch.tensor(position_offsets, dtype=torch.int64, device=dev)
         lk = torch.tensor([L + 1 for L in lens], dtype=torch.int32, device=dev)
+        bt, mb = pool["bt"], pool["mb"]
         bps = self.decode_blocks_per_split
         ws = self._workspace(B, mb, bps)
         x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
         new = [[] for _ in range(B)]
         short = [b for b in range(B) if lens[b] < max_len]
+        idx = torch.tensor([slots_host[b] for b in short], device=dev) if short else None
+
         def attention(li, layer, h):
+            kbuf, vbuf = kbufs[li], vbufs[li]
+            kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
+            q, k, v = self._qkv(layer, h)
+            ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
+            attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,
+                                              out_layout=self.decode_layout)
+            if self.reference_compat and short:
+                kf[idx] = 0
+                vf[idx] = 0
+            for b in range(B):
+                s0 = starts[b] * BS
+                new[b].append((kf[s0:s0 + lens[b] + 1], vf[s0:s0 + lens[b] + 1]))
+            return attn
+
+        h = self._run_layers(x, attention)
+        pool["lens"] = [L + 1 for L in lens]
+        pool["ptrs"] = [new[b][0][0].data_ptr() for b in range(B)]
+        assert len(new[0]) == L_layers
+        return self._logits(h), new
+
+    def _batch_pool_matches(self, pool, kv_caches, lens) -> bool:
+        """The caches are exactly the views the last call returned (checked on every
+        layer's K and V by address and length) and every sequence has room for one more
+        token in its run."""
+        if pool["lens"] != lens:
+            return False
+        kp, vp = pool["k_ptrs"], pool["v_ptrs"]
+        for b, cache in enumerate(kv_caches):
+            if lens[b] + 1 > pool["cap"][b] * BS:
+                return False
+            for li, (k, v) in enumerate(cache):
+                if k.data_ptr() != kp[li][b] or v.data_ptr() != vp[li][b]:
+                    return False
+        return True
+
+    def _pack_batch(self, kv_caches, lens) -> dict:
+        """New per-layer block buffers holding every sequence's history (one
+        multi-tensor copy per layer) with decode_batch_headroom free tokens after it."""
+        dev = self.device
+        B = len(lens)
+        cap = [(L + 1 + self.decode_batch_headroom + BS - 1) // BS for L in lens]
+        starts = [0]
+        for n in cap[:-1]:
+            starts.append(starts[-1] + n)
+        total_blocks = starts[-1] + cap[-1]
+        mb = max(cap)
+        bt_host = torch.zeros(B, mb, dtype=torch.int32)
+        for b in range(B):
+            bt_host[b, :cap[b]] = torch.arange(starts[b], starts[b] + cap[b], dtype=torch.int32)
+        kbufs, vbufs = [], []
+        elt = torch.empty(0, dtype=self.dtype).element_size()
+        row = self.Kh * self.D * elt
+        for li in range(len(self.layers)):
             kbuf = torch.zeros(total_blocks, BS, self.Kh, self.D, dtype=self.dtype, device=dev)
             vbuf = torch.zeros_like(kbuf)
             kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
-            # every sequence's history into its blocks: one multi-tensor copy per layer
-            # instead of two copies per sequence
             dst = [kf[starts[b] * BS:starts[b] * BS + lens[b]] for b in range(B) if lens[b]]
             dst += [vf[starts[b] * BS:starts[b] * BS + lens[b]] for b in range(B) if lens[b]]
             src = [kv_caches[b][li][0] for b in range(B) if lens[b]]
             src += [kv_caches[b][li][1] for b in range(B) if lens[b]]
             if dst:
                 torch._foreach_copy_(dst, [t.to(device=dev) for t in src])
-            q, k, v = self._qkv(layer, h)
-            ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
-            attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,
-                                              out_layout=self.decode_layout)
-            if self.reference_compat and short:
-                idx = torch.tensor([slots_host[b] for b in short], device=dev)
-                kf[idx] = 0
-                vf[idx] = 0
-            for b in range(B):
-                s = starts[b] * BS
-                new[b].append((kf[s:s + lens[b] + 1], vf[s:s + lens[b] + 1]))
-            return attn
-
-        h = self._run_layers(x, attention)
-        return self._logits(h), new
+            kbufs.append(kbuf)
+            vbufs.append(vbuf)
+        k_ptrs = [[kbufs[li].data_ptr() + starts[b] * BS * row for b in range(B)]
+                  for li in range(len(self.layers))]
+        v_ptrs = [[vbufs[li].data_ptr() + starts[b] * BS * row for b in range(B)]
+                  for li in range(len(self.layers))]
+        return {"B": B, "starts": starts, "cap": cap, "k": kbufs, "v": vbufs,
+                "bt": bt_host.to(dev), "mb": mb, "lens": None, "k_ptrs": k_ptrs,
+                "v_ptrs": v_ptrs}
 
     # ------------------------------------------------------------------ decode (paged)
     def _decode_core(self, tokens: torch.Tensor, seq_lens: torch.Tensor, row_ids: torch.Tensor,

@@ -458,3 +458,48 @@ def test_graphed_decode_config2_shape_bf16_vs_oracle_256_steps():
     (km, ka, kd), (om, oa, od) = stats["kernels"], stats["oracle_bf16"]
     assert km <= 1.5 * om and ka <= 1.5 * oa
     assert kd <= 1.5 * od + 8
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_batch_reuses_its_buffers_with_the_same_results(dtype):
+    """forward_decode_batch fed its own returned caches works in place (only the new
+    token written) and must give the logits and caches of a call that packs every
+    history afresh, bit for bit, across block boundaries, a run that fills up (headroom
+    of 20 tokens), the reference's zero row for shorter sequences, and a batch change."""
+    cfg = ModelConfig(hidden_dim=256, n_heads=8, n_kv_heads=2, n_layers=2, vocab_size=512,
+                      max_seq_len=4096, intermediate_size=512, rope_theta=500000.0)
+    m = b200_model(cfg, dtype=dtype, fused=True)
+    m.decode_batch_headroom = 20
+    m.decode_blocks_per_split = 4  # the same split-K decomposition in both layouts
+    g = torch.Generator().manual_seed(3)
+    lens0 = [1, 15, 16, 33, 300]
+    caches = [[(torch.randn(L, 2, 32, generator=g).to(dtype).to(DEV),
+                torch.randn(L, 2, 32, generator=g).to(dtype).to(DEV)) for _ in range(2)]
+              for L in lens0]
+    last = torch.randint(3, 512, (5,), generator=g).tolist()
+    pos = list(lens0)
+    packs = 0
+    orig = m._pack_batch
+
+    def counting(*a):
+        nonlocal packs
+        packs += 1
+        return orig(*a)
+    m._pack_batch = counting
+    for step in range(30):
+        if step == 20:  # the batch changes: request 1 leaves
+            caches, last, pos = caches[:1] + caches[2:], last[:1] + last[2:], pos[:1] + pos[2:]
+        lg, new = m.forward_decode_batch(last, caches, pos)
+        saved = m._batch_pool
+        m._batch_pool = None  # the same call with every history packed afresh
+        lg2, new2 = m.forward_decode_batch(last, [[(k.clone(), v.clone()) for k, v in c]
+                                                  for c in caches], pos)
+        m._batch_pool = saved
+        assert torch.equal(lg, lg2), step
+        for c1, c2 in zip(new, new2):
+            for (k1, v1), (k2, v2) in zip(c1, c2):
+                assert torch.equal(k1, k2) and torch.equal(v1, v2), step
+        caches, last, pos = new, lg.argmax(-1).tolist(), [x + 1 for x in pos]
+    # repacks: the first call, when the longest-run sequence fills its headroom, and at
+    # the batch change; every other step reused the buffers
+    assert 2 <= packs - 30 <= 6, packs
