@@ -423,6 +423,9 @@ class B200LlamaModel(nn.Module):
         new = [[] for _ in range(B)]
         short = [b for b in range(B) if lens[b] < max_len]
         idx = torch.tensor([slots_host[b] for b in short], device=dev) if short else None
+        sizes = []  # run b: its L_b + 1 tokens, then the rest of its blocks
+        for b in range(B):
+            sizes += [lens[b] + 1, pool["cap"][b] * BS - lens[b] - 1]
 
         def attention(li, layer, h):
             kbuf, vbuf = kbufs[li], vbufs[li]
@@ -434,9 +437,10 @@ class B200LlamaModel(nn.Module):
             if self.reference_compat and short:
                 kf[idx] = 0
                 vf[idx] = 0
+            # every sequence's [history + new token] view in one split per buffer
+            ks, vs = kf.split(sizes)[0::2], vf.split(sizes)[0::2]
             for b in range(B):
-                s0 = starts[b] * BS
-                new[b].append((kf[s0:s0 + lens[b] + 1], vf[s0:s0 + lens[b] + 1]))
+                new[b].append((ks[b], vs[b]))
             return attn
 
         h = self._run_layers(x, attention)
