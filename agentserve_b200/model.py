@@ -411,43 +411,88 @@ class B200LlamaModel(nn.Module):
         pool = self._batch_pool
         if not (pool is not None and pool["B"] == B and self._batch_pool_matches(pool, kv_caches, lens)):
             pool = self._batch_pool = self._pack_batch(kv_caches, lens)
-        starts, kbufs, vbufs = pool["starts"], pool["k"], pool["v"]
+        starts = pool["starts"]
         slots_host = [starts[b] * BS + lens[b] for b in range(B)]
-        slots = torch.tensor(slots_host, dtype=torch.int64, device=dev)
-        pos = torch.tensor(position_offsets, dtype=torch.int64, device=dev)
-        lk = torch.tensor([L + 1 for L in lens], dtype=torch.int32, device=dev)
-        bt, mb = pool["bt"], pool["mb"]
-        bps = self.decode_blocks_per_split
-        ws = self._workspace(B, mb, bps)
-        x = self.embed(torch.tensor(last_token_ids, dtype=torch.long, device=dev))
-        new = [[] for _ in range(B)]
         short = [b for b in range(B) if lens[b] < max_len]
-        idx = torch.tensor([slots_host[b] for b in short], device=dev) if short else None
+        st = pool.get("static")
+        if st is not None and st["bps"] != self.decode_blocks_per_split:
+            st = None  # the workspace and any captured step follow the split size
+            pool.pop("graph", None)
+        if st is None:  # the step's inputs, staged with one copy per call
+            n = 4 * B + len(short)
+            host = torch.zeros(n, dtype=torch.int64).pin_memory()
+            buf = torch.zeros(n, dtype=torch.int64, device=dev)
+            st = pool["static"] = {
+                "host": host, "np": host.numpy(), "buf": buf, "copied": torch.cuda.Event(),
+                "tokens": buf[:B], "pos": buf[B:2 * B], "slots": buf[2 * B:3 * B],
+                "lk": buf[3 * B:4 * B], "idx": buf[4 * B:], "n_short": len(short),
+                "bps": self.decode_blocks_per_split,
+                "ws": ops.new_decode_workspace(B, self.H, self.Kh, self.D, pool["mb"],
+                                               self.decode_blocks_per_split, dev)}
+        assert st["n_short"] == len(short)
+        st["copied"].synchronize()  # the previous call's copy has left the pinned buffer
+        h_np = st["np"]
+        h_np[:B] = last_token_ids
+        h_np[B:2 * B] = position_offsets
+        h_np[2 * B:3 * B] = slots_host
+        h_np[3 * B:4 * B] = [L + 1 for L in lens]
+        h_np[4 * B:] = [slots_host[b] for b in short]
+        st["buf"].copy_(st["host"], non_blocking=True)
+        st["copied"].record()
+
+        graphed = self.decode_graphs and dev.type == "cuda"
+        if graphed and pool.get("graph") is None and pool.get("calls", 0) >= 1:
+            # the first call on these buffers ran eagerly (lazy initialisation); capture,
+            # in a memory pool of the graph's own (the graph goes when the buffers do)
+            pool["mempool"] = torch.cuda.graph_pool_handle()
+            s_ = torch.cuda.Stream(device=dev)
+            s_.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=pool["mempool"], stream=s_,
+                                  capture_error_mode="relaxed"):
+                pool["logits"] = self._decode_batch_body(pool)
+            torch.cuda.current_stream().wait_stream(s_)
+            pool["graph"] = graph
+        if graphed and pool.get("graph") is not None:
+            pool["graph"].replay()
+            logits = pool["logits"].clone()
+        else:
+            logits = self._decode_batch_body(pool)
+        pool["calls"] = pool.get("calls", 0) + 1
+
+        # every sequence's [history + new token] view, one split per buffer
         sizes = []  # run b: its L_b + 1 tokens, then the rest of its blocks
         for b in range(B):
             sizes += [lens[b] + 1, pool["cap"][b] * BS - lens[b] - 1]
+        views_k = [kb.view(-1, self.Kh, self.D).split(sizes)[0::2] for kb in pool["k"]]
+        views_v = [vb.view(-1, self.Kh, self.D).split(sizes)[0::2] for vb in pool["v"]]
+        new = [[(views_k[li][b], views_v[li][b]) for li in range(L_layers)] for b in range(B)]
+        pool["lens"] = [L + 1 for L in lens]
+        return logits, new
+
+    def _decode_batch_body(self, pool) -> torch.Tensor:
+        """forward_decode_batch's device work on the staged inputs of `pool` (no host
+        reads: also the body of its captured graph)."""
+        st = pool["static"]
+        bps = self.decode_blocks_per_split
+        lk = st["lk"].to(torch.int32)
+        x = self.embed(st["tokens"])
 
         def attention(li, layer, h):
-            kbuf, vbuf = kbufs[li], vbufs[li]
-            kf, vf = kbuf.view(-1, self.Kh, self.D), vbuf.view(-1, self.Kh, self.D)
+            kbuf, vbuf = pool["k"][li], pool["v"][li]
             q, k, v = self._qkv(layer, h)
-            ops.rope_reshape_and_cache(q, k, v, pos, slots, self.rope_table, kbuf, vbuf)
-            attn = ops.paged_decode_attention(q, kbuf, vbuf, bt, lk, self.scale, bps, ws,
-                                              out_layout=self.decode_layout)
-            if self.reference_compat and short:
-                kf[idx] = 0
-                vf[idx] = 0
-            # every sequence's [history + new token] view in one split per buffer
-            ks, vs = kf.split(sizes)[0::2], vf.split(sizes)[0::2]
-            for b in range(B):
-                new[b].append((ks[b], vs[b]))
+            ops.rope_reshape_and_cache(q, k, v, st["pos"], st["slots"], self.rope_table, kbuf,
+                                       vbuf)
+            attn = ops.paged_decode_attention(q, kbuf, vbuf, pool["bt"], lk, self.scale, bps,
+                                              st["ws"], out_layout=self.decode_layout)
+            if self.reference_compat and st["n_short"]:
+                # the reference returns a zero K/V row as the new token of every sequence
+                # shorter than the batch's longest (llama.py:327, 372)
+                kbuf.view(-1, self.Kh, self.D).index_fill_(0, st["idx"], 0)
+                vbuf.view(-1, self.Kh, self.D).index_fill_(0, st["idx"], 0)
             return attn
 
-        h = self._run_layers(x, attention)
-        pool["lens"] = [L + 1 for L in lens]
-        pool["ptrs"] = [new[b][0][0].data_ptr() for b in range(B)]
-        assert len(new[0]) == L_layers
-        return self._logits(h), new
+        return self._logits(self._run_layers(x, attention))
 
     def _batch_pool_matches(self, pool, kv_caches, lens) -> bool:
         """The caches are exactly the views the last call returned (checked on every
@@ -647,6 +692,8 @@ class B200LlamaModel(nn.Module):
             g.release()
         self._graphs.clear()
         self._graph_pool = None
+        if self._batch_pool is not None and self._batch_pool.get("graph") is not None:
+            self._batch_pool.pop("graph").reset()  # forward_decode_batch's captured step
 
 
 def _batch_bucket(B: int) -> int:
