@@ -142,3 +142,44 @@ def test_zero_copy_prefix_sharing_ref_counts(alloc):
     alloc.allocate("E", 1)
     with pytest.raises(ValueError):
         alloc.share_blocks("E", alloc.blocks_for("E"))  # must share before allocating
+
+
+def test_decode_batch_buffers_layout_and_reuse_rules():
+    """forward_decode_batch's host bookkeeping (no kernel runs): each sequence's
+    history is copied into its own run of blocks with the headroom after it, the
+    returned-view addresses are recorded per layer, and a later call may reuse the
+    buffers only with exactly those views, the same lengths and room left."""
+    from agentserve_b200 import B200LlamaModel
+    from agentserve_b200.config import ModelConfig
+    cfg = ModelConfig(hidden_dim=64, n_heads=4, n_kv_heads=2, n_layers=2, vocab_size=100,
+                      max_seq_len=512, intermediate_size=128)
+    m = B200LlamaModel(cfg, dtype=torch.float32, device="cpu")
+    m.decode_batch_headroom = 20
+    lens = [0, 5, 16, 40]
+    g = torch.Generator().manual_seed(0)
+    caches = [[(torch.randn(L, 2, 16, generator=g), torch.randn(L, 2, 16, generator=g))
+               for _ in range(2)] for L in lens]
+    pool = m._pack_batch(caches, lens)
+    assert pool["cap"] == [(L + 1 + 20 + 15) // 16 for L in lens]
+    assert pool["starts"] == [0, 2, 4, 7]
+    row = 2 * 16 * 4  # Kh * D * 4 bytes
+    for li in range(2):
+        kf = pool["k"][li].view(-1, 2, 16)
+        for b, L in enumerate(lens):
+            s0 = pool["starts"][b] * 16
+            assert torch.equal(kf[s0:s0 + L], caches[b][li][0])
+            assert pool["k_ptrs"][li][b] == pool["k"][li].data_ptr() + s0 * row
+            assert int(pool["bt"][b, 0]) == pool["starts"][b]
+    # the views the call would return (history + new token) match; anything else not
+    pool["lens"] = [L + 1 for L in lens]
+    views = [[(pool["k"][li].view(-1, 2, 16)[pool["starts"][b] * 16:][:L + 1],
+               pool["v"][li].view(-1, 2, 16)[pool["starts"][b] * 16:][:L + 1])
+              for li in range(2)] for b, L in enumerate(lens)]
+    assert m._batch_pool_matches(pool, views, pool["lens"])
+    assert not m._batch_pool_matches(pool, views, lens)                      # other lengths
+    assert not m._batch_pool_matches(pool, views[::-1], pool["lens"][::-1])  # other order
+    moved = [list(c) for c in views]
+    moved[2][1] = (moved[2][1][0].clone(), moved[2][1][1])                   # one copied view
+    assert not m._batch_pool_matches(pool, moved, pool["lens"])
+    full = dict(pool, lens=[pool["cap"][0] * 16] + pool["lens"][1:])        # a full run
+    assert not m._batch_pool_matches(full, views, full["lens"])
