@@ -244,7 +244,7 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
 def rope_decode_fusable(q: torch.Tensor, k_cache: torch.Tensor) -> bool:
     """True when rope_paged_decode_attention's one-launch path applies (bf16 / fp16,
     head_dim 64 or 128, at most 8 query heads per KV head)."""
-    B, H, D = q.shape
+    _, H, D = q.shape
     Kh = k_cache.shape[2]
     return (q.dtype in (torch.bfloat16, torch.float16) and D in (64, 128) and H % Kh == 0
             and H // Kh <= 8)
@@ -446,7 +446,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
         out = torch.empty_like(x)
     _require(out.shape == x.shape and out.dtype == x.dtype and out.is_contiguous(),
              "rmsnorm: out must be a contiguous tensor like x")
-    rows, dim = x.shape[0], x.shape[-1]
+    dim = x.shape[-1]
     N.check(N.load().as_rmsnorm(_ptr(out), _ptr(x), _ptr(weight), x.numel() // dim, dim,
                                 float(eps), dtype_code(x.dtype), _stream(x.device)), "as_rmsnorm")
     return out

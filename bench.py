@@ -209,7 +209,7 @@ def cpu_baseline(args, steps: int, warmup: int, seqs: int):
     m = OracleLlama(cfg)
     g = torch.Generator().manual_seed(1234)
     with torch.no_grad():
-        for n, p in m.named_parameters():
+        for p in m.parameters():
             if p.dim() == 2:
                 p.normal_(0.0, 0.02, generator=g)
     m.eval()
