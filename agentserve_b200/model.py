@@ -441,9 +441,10 @@ class B200LlamaModel(nn.Module):
         st["copied"].record()
 
         graphed = self.decode_graphs and dev.type == "cuda"
-        if graphed and pool.get("graph") is None and pool.get("calls", 0) >= 1:
-            # the first call on these buffers ran eagerly (lazy initialisation); capture,
-            # in a memory pool of the graph's own (the graph goes when the buffers do)
+        if graphed and pool.get("graph") is None and pool.get("calls", 0) >= 2:
+            # the first calls on these buffers ran eagerly (lazy initialisation, and a
+            # batch that changes again at once is not worth a capture); capture, in a
+            # memory pool of the graph's own (the graph goes when the buffers do)
             pool["mempool"] = torch.cuda.graph_pool_handle()
             s_ = torch.cuda.Stream(device=dev)
             s_.wait_stream(torch.cuda.current_stream())
